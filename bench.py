@@ -1,0 +1,492 @@
+#!/usr/bin/env python3
+"""Benchmark: whole-box Transformer inference forward tokens/s on B200.
+
+Workload (default): BASELINE config C2 -- fp32, B=8, S=2048, d_model=1024,
+H=16 (head_dim 64), FFN 4096 with GELU, 4 pre-LN layers, causal; random
+default-initialised weights (torch.manual_seed(0)) and x ~ N(0, 1). One step
+is one forward of UserOptimizedTransformer over one batch. Under torchrun
+each GPU runs its own batch of 8 sequences (weak scaling, no collective on
+the hot path); the reported value is all ranks' tokens / max-over-ranks time.
+
+Printed JSON line (rank 0): value (device-resident inputs), e2e (pinned host
+input -> forward -> host output, copies inside the timed region), the
+attention roofline (algorithmic FLOPs / CUDA-event launch time, live), the
+LayerNorm bandwidth, the CPU baseline (the explicit-attention model of the
+reference restated in oracle/, on the host cores), SM clocks sampled during
+the timed region, and the number of libb200tk kernels launched.
+
+``--impl reference`` times the reference's explicit-attention forward on the
+host CPU cores (rank 0 only; other ranks exit 0) on a bounded sample of the
+same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "triton-transformer-kernels_b200"))
+
+CONFIGS = {
+    # name: (batch, seq, d_model, heads, ffn, layers, causal, dtype)
+    "C1": (2, 128, 256, 4, 1024, 1, False, "float32"),
+    "C2": (8, 2048, 1024, 16, 4096, 4, True, "float32"),
+    "C3": (4, 16384, 4096, 32, 16384, 1, True, "bfloat16"),
+    "C4": (4, 512, 4096, 32, 16384, 2, False, "float32"),
+    "C5": (512, 512, 768, 12, 3072, 12, False, "bfloat16"),
+}
+DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16}
+DTYPE_TAG = {"float32": "f32", "bfloat16": "bf16"}
+METRIC = "forward tokens/s (whole box)"
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+# DRAM bytes per attention launch (dram__bytes_read.sum + dram__bytes_write.sum)
+# from one ncu capture of the same kernel and workload; see profiles/.
+NCU_ATTENTION_TRAFFIC = {}
+
+
+def describe(name: str) -> str:
+    b, s, d, h, f, layers, causal, dt = CONFIGS[name]
+    return (
+        f"{name}: {dt} B{b} S{s} d_model{d} H{h} head_dim{d // h} FFN{f} "
+        f"L{layers} {'causal' if causal else 'non-causal'}"
+    )
+
+
+def attention_flops(b: int, s: int, h: int, d: int, causal: bool) -> float:
+    """Algorithmic FLOPs of one attention launch (2 per multiply-add, QK^T + PV).
+    Causal counts the S(S+1)/2 allowed (query, key) pairs."""
+    return 2.0 * b * h * d * s * (s + 1) if causal else 4.0 * b * h * s * s * d
+
+
+def load_peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {
+            "hbm_gbs": float(data["hbm_gbs"]),
+            "bf16_tflops": float(data["bf16_tflops"]),
+            "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained", data["bf16_tflops"])),
+            "source": "measured",
+        }
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle-reason samples while the timed region runs."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, sm_max, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": sm_max,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+class LaunchTimer:
+    """CUDA-event timing of each libb200tk launch on the stream it runs on."""
+
+    def __init__(self) -> None:
+        self.enabled = False
+        self.pairs = {"attention": [], "rln": []}
+        self.launches = 0
+
+    def wrap(self, native):
+        timer = self
+        orig_attn, orig_rln = native.attention_fwd, native.residual_layer_norm_fwd
+
+        def timed(kind, fn):
+            def inner(*args, **kwargs):
+                timer.launches += 1
+                if not timer.enabled:
+                    return fn(*args, **kwargs)
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record()
+                result = fn(*args, **kwargs)
+                end.record()
+                # keep sizes only: holding the tensors would pin every step's activations
+                x = args[0]
+                meta = (x.numel(), x.element_size(), x.shape[-1], args[1] is None)
+                timer.pairs[kind].append((start, end, meta))
+                return result
+            return inner
+
+        native.attention_fwd = timed("attention", orig_attn)
+        native.residual_layer_norm_fwd = timed("rln", orig_rln)
+
+    def mean_ms(self, kind: str) -> float:
+        times = [s.elapsed_time(e) for s, e, _ in self.pairs[kind]]
+        return sum(times) / len(times) if times else float("nan")
+
+    def rln_bytes_per_launch(self) -> float:
+        total = 0.0
+        for _, _, (numel, elem, width, no_update) in self.pairs["rln"]:
+            # read x (+ update), write normalized (+ residual), plus gamma/beta
+            tensors = 2 if no_update else 4
+            total += tensors * numel * elem + 2 * width * elem
+        return total / max(1, len(self.pairs["rln"]))
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+class CpuReference:
+    """The reference's explicit-attention model (its restatement in oracle/)
+    on the host CPU cores; one forward of one sequence of the workload is the
+    bounded sample (sequences are independent, so tokens/s carries over)."""
+
+    def __init__(self, name: str) -> None:
+        from oracle import explicit as oracle
+
+        b, s, d, h, f, layers, causal, dt = CONFIGS[name]
+        self.name, self.batch, self.seq = name, b, s
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        cfg = oracle.TransformerConfig(1, s, d, h, f, layers, causal)
+        torch.manual_seed(0)
+        self.model = oracle.BaselineTransformer(cfg).to(DTYPES[dt]).eval()
+        self.x, _ = oracle.generate_random_case(cfg, torch.device("cpu"), DTYPES[dt], 1)
+
+    def forward_seconds(self) -> float:
+        with torch.inference_mode():
+            t0 = time.perf_counter_ns()
+            self.model(self.x)
+            return (time.perf_counter_ns() - t0) / 1e9
+
+    def describe(self, times) -> dict:
+        median = statistics.median(times)
+        return {
+            "value": self.seq / median,
+            "unit": "tokens/s",
+            "cores": self.threads,
+            "kind": "port",
+            "sample": (
+                f"oracle BaselineTransformer (explicit attention, torch CPU, "
+                f"{self.threads} threads): 1 of {self.batch} sequences of {self.name} "
+                f"({self.seq} tokens) per forward, {len(times)} timed forwards, "
+                f"median {median:.3f} s"
+            ),
+        }
+
+
+def cpu_reference_throughput(name: str, budget_s: float = 15.0) -> dict:
+    """Bounded CPU-baseline sample: forwards until ~budget_s of CPU work (>= 2)."""
+    ref = CpuReference(name)
+    ref.forward_seconds()  # warm-up
+    times, start = [], time.perf_counter()
+    while len(times) < 2 or time.perf_counter() - start < budget_s:
+        times.append(ref.forward_seconds())
+        if time.perf_counter() - start > 2 * budget_s:
+            break
+    return ref.describe(times)
+
+
+def run_reference_arm(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    name = args.config
+    ref = CpuReference(name)
+    for _ in range(args.warmup):
+        ref.forward_seconds()
+    times = [ref.forward_seconds() for _ in range(max(1, args.steps))]
+    base = ref.describe(times)
+    value = base["value"]
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * statistics.median(times),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": DTYPE_TAG[CONFIGS[name][-1]],
+        "data": "synthetic (x ~ N(0,1); default init, torch.manual_seed(0))",
+        "config": {"workload": describe(name), "global_batch": 1, "seq_len": ref.seq,
+                   "parallelism": "host CPU cores (rank 0 only)"},
+        "cpu_baseline": base,
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200_arm(args) -> int:
+    from oracle import explicit as oracle  # checker + CPU baseline only
+    from transformer_opt.kernels import _native
+    from transformer_opt.submission import TransformerConfig, UserOptimizedTransformer
+
+    world, rank, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    name = args.config
+    b, s, d, h, f, layers, causal, dt = CONFIGS[name]
+    dtype = DTYPES[dt]
+    torch.backends.cuda.matmul.allow_tf32 = True  # the harness's flags
+    torch.backends.cudnn.allow_tf32 = True
+    torch.set_float32_matmul_precision("high")
+
+    timer = LaunchTimer()
+    timer.wrap(_native)
+
+    torch.manual_seed(0)
+    model = UserOptimizedTransformer(TransformerConfig(b, s, d, h, f, layers, causal))
+    model = model.to(device=device, dtype=dtype).eval()
+    cfg = oracle.TransformerConfig(b, s, d, h, f, layers, causal)
+    x, _ = oracle.generate_random_case(cfg, device, dtype, 1 + rank)  # this rank's batch
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    with torch.inference_mode():
+        # warm-up (also builds packed projection weights)
+        for _ in range(args.warmup):
+            model(x)
+        torch.cuda.synchronize(device)
+        _native.device_status(local, clear=True)
+
+        # ---- device-resident timed region
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        launches_before = timer.launches
+        timer.enabled = True
+        barrier(world)
+        torch.cuda.synchronize(device)
+        with ClockSampler(local) as clocks:
+            for i in range(args.steps):
+                flush.zero_()  # evict the previous step's data from L2
+                starts[i].record(stream)
+                model(x)
+                ends[i].record(stream)
+            torch.cuda.synchronize(device)
+            barrier(world)
+        timer.enabled = False
+        launches = timer.launches - launches_before
+        step_ms = [st.elapsed_time(en) for st, en in zip(starts, ends)]
+        local_ms = sum(step_ms) / len(step_ms)
+        from transformer_opt.sharding import gather_stats, max_over_ranks
+
+        ms_per_step = max_over_ranks(local_ms, device)
+        attn_ms = timer.mean_ms("attention")
+        rln_ms = timer.mean_ms("rln")
+        rln_bytes = timer.rln_bytes_per_launch()
+
+        # ---- end-to-end through the public API with host buffers
+        x_host = x.cpu().pin_memory()
+        y_host = torch.empty(x.shape, dtype=dtype).pin_memory()
+        x_dev = torch.empty_like(x)
+        e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier(world)
+        torch.cuda.synchronize(device)
+        for i in range(args.steps):
+            flush.zero_()
+            e_starts[i].record(stream)
+            x_dev.copy_(x_host, non_blocking=True)
+            y = model(x_dev)
+            y_host.copy_(y, non_blocking=True)
+            e_ends[i].record(stream)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        e2e_local = sum(a.elapsed_time(b_) for a, b_ in zip(e_starts, e_ends)) / args.steps
+        e2e_ms = max_over_ranks(e2e_local, device)
+        status = _native.device_status(local)
+
+        # ---- validation (outside the timed regions): this rank vs the oracle
+        valid_ok, max_err = 1.0, 0.0
+        if args.validate:
+            torch.manual_seed(0)
+            baseline = oracle.BaselineTransformer(cfg).to(device=device, dtype=dtype).eval()
+            oracle.copy_model_weights(model, baseline, strict=True)
+            ref = baseline(x)
+            res = oracle.compare_outputs(ref, y)
+            valid_ok, max_err = (1.0 if res.passed else 0.0), res.max_abs_error
+            del baseline, ref
+        per_rank = gather_stats([valid_ok, max_err, float(status)], device)
+
+    tokens = world * b * s
+    value = tokens / (ms_per_step / 1000.0)
+    peaks = load_peaks()
+    flops = attention_flops(b, s, h, d // h, causal)
+    achieved_tflops = flops / (attn_ms / 1000.0) / 1e12
+    peak_tf = peaks["bf16_tflops_sustained"]
+    roofline = {
+        "bound": "tensor",
+        "kernel": "attention_fwd_tc_kernel",
+        "achieved": achieved_tflops,
+        "peak": peak_tf,
+        "unit": "TFLOP/s",
+        "frac": achieved_tflops / peak_tf,
+        "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+        "traffic": NCU_ATTENTION_TRAFFIC.get(name),
+        "flops_per_launch": flops,
+        "launch_ms": attn_ms,
+    }
+    if dtype == torch.float32:
+        # 3xTF32: three TF32 MMAs per product; the TF32 rate is half the bf16
+        # rate, so the fp32 path's tensor ceiling is peak / 6.
+        roofline["note"] = "fp32 runs 3xTF32: tensor-core ceiling = bf16 peak / 6"
+        roofline["frac_of_3xtf32_ceiling"] = achieved_tflops / (peak_tf / 6.0)
+    rln_gbs = rln_bytes / (rln_ms / 1000.0) / 1e9
+    line = {
+        "impl": "b200",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": DTYPE_TAG[dt],
+        "data": "synthetic (x ~ N(0,1); default init, torch.manual_seed(0))",
+        "config": {
+            "workload": describe(name),
+            "model": f"pre-LN Transformer encoder, {layers} layers",
+            "global_batch": world * b,
+            "seq_len": s,
+            "parallelism": f"dp{world} (batch shards, weights replicated, no collective)",
+            "l2": "flushed between timed steps (256 MiB write)",
+        },
+        "e2e": {
+            "value": tokens / (e2e_ms / 1000.0),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": x.numel() * x.element_size(),
+            "d2h_bytes_per_step": x.numel() * x.element_size(),
+        },
+        "roofline": roofline,
+        "rln": {
+            "bound": "hbm",
+            "achieved": rln_gbs,
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": rln_gbs / peaks["hbm_gbs"],
+            "launch_ms": rln_ms,
+            "bytes_per_launch": rln_bytes,
+        },
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "validation": {
+            "all_ranks_pass": all(r[0] == 1.0 for r in per_rank),
+            "max_abs_error": max(r[1] for r in per_rank),
+            "device_status": [int(r[2]) for r in per_rank],
+        },
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference_throughput(name, budget_s=args.ref_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--config", choices=sorted(CONFIGS), default="C2")
+    parser.add_argument("--no-validate", dest="validate", action="store_false")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--ref-budget", type=float, default=15.0,
+                        help="seconds of CPU work per reference sample")
+    args = parser.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        parser.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_b200_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

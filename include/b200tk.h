@@ -1,0 +1,144 @@
+/*
+ * b200tk.h - C ABI of libb200tk.so, the sm_100a (B200) kernels behind the
+ * Transformer inference hot path: fused attention forward and fused
+ * residual-add + LayerNorm.
+ *
+ * Every entry point takes plain device pointers, element strides, sizes and a
+ * cudaStream_t passed as void*. Nothing here allocates device memory, blocks
+ * the host, or depends on PyTorch, so each call is safe inside CUDA-graph
+ * capture once the library has been initialised on the device (the first
+ * call on a device resolves the status-word address; make it outside capture).
+ *
+ * Return value: B200TK_OK or a negative B200TK_ERR_* code. The message for
+ * the most recent failure on the calling thread is b200tk_last_error().
+ * Device-side pipeline timeouts are not return codes: they are recorded in a
+ * per-device status word that b200tk_device_status() reads.
+ *
+ * The reference implements these two operations as Triton kernels behind
+ * Python wrappers; it has no C ABI. The citations below name the reference
+ * function each entry point replaces (paths inside the reference project).
+ */
+#ifndef B200TK_H
+#define B200TK_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200TK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define B200TK_API __attribute__((visibility("default")))
+#else
+#define B200TK_API
+#endif
+
+/* Return codes. */
+#define B200TK_OK 0
+#define B200TK_ERR_INVALID_ARGUMENT (-1) /* shapes, strides, pointers, flags */
+#define B200TK_ERR_UNSUPPORTED (-2)      /* valid but outside the kernel envelope */
+#define B200TK_ERR_CUDA (-3)             /* a CUDA runtime/driver call failed */
+
+/* Element types. */
+#define B200TK_DTYPE_FLOAT32 0
+#define B200TK_DTYPE_FLOAT16 1
+#define B200TK_DTYPE_BFLOAT16 2
+
+/* Residual LayerNorm flags (bit set). */
+#define B200TK_RLN_ZERO_INVALID_RESIDUAL 1u   /* residual_out row := 0 where mask is false */
+#define B200TK_RLN_ZERO_INVALID_NORMALIZED 2u /* normalized_out row := 0 where mask is false */
+#define B200TK_RLN_NO_UPDATE 4u               /* plain LayerNorm: update and residual_out unused */
+
+/* Device status bits (b200tk_device_status). */
+#define B200TK_STATUS_PIPELINE_TIMEOUT 1u /* an mbarrier wait hit its iteration/time limit */
+#define B200TK_STATUS_SELFTEST_TIMEOUT 2u /* set only by b200tk_selftest_wait_timeout */
+
+/* Attention kernel routes reported by b200tk_attention_route. */
+#define B200TK_ROUTE_TCGEN05 1 /* TMA + tcgen05.mma + TMEM pipeline */
+#define B200TK_ROUTE_GENERIC 2 /* CUDA-core kernel for shapes outside the tcgen05 envelope */
+
+/* ABI version of the loaded library (B200TK_ABI_VERSION at build time). */
+B200TK_API int b200tk_abi_version(void);
+
+/* Human-readable message for the last failed call on this host thread. */
+B200TK_API const char* b200tk_last_error(void);
+
+/*
+ * Fused attention forward: out = softmax(scale * q k^T + masks) v, per
+ * (batch, head), without materialising the score matrix.
+ *
+ * Replaces: transformer_opt/kernels/attention.py:268-360 (triton_attention,
+ * launching _attention_fwd at :103-265). Semantics follow the explicit
+ * reference math, transformer_opt/dispatch.py:69-96.
+ *
+ * q, k, v : [batch, seq_len, heads, head_dim] in `dtype`, arbitrary element
+ *           strides for the first three dims (packed QKV views included);
+ *           the head_dim stride must be 1. Strides are given as 3 int64
+ *           element strides {batch, seq, head}.
+ * valid_token_mask : optional [batch, seq_len] bool (1 byte per element,
+ *           strides {batch, seq} in elements); NULL means all keys valid.
+ *           A false entry removes that key for every query.
+ * out     : contiguous [batch, seq_len, heads, head_dim] in `dtype`.
+ * causal  : nonzero applies the key <= query constraint.
+ * scale   : multiplies q k^T (head_dim^-0.5 in the model).
+ * Rows whose keys are all masked produce zeros.
+ * head_dim in {8, 16, 32, 64, 128}; dtype float32 runs a 3xTF32 split on the
+ * tensor cores, float16/bfloat16 run native f16-kind MMAs with fp32
+ * accumulation.
+ */
+B200TK_API int b200tk_attention_fwd(const void* q, const int64_t* q_strides, const void* k,
+                         const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                         const uint8_t* valid_token_mask, const int64_t* mask_strides,
+                         void* out, int dtype, int64_t batch, int64_t seq_len, int64_t heads,
+                         int64_t head_dim, int causal, float scale, void* stream);
+
+/*
+ * Which kernel b200tk_attention_fwd would launch for these arguments
+ * (B200TK_ROUTE_*), or a negative error code. Pure host-side query.
+ */
+B200TK_API int b200tk_attention_route(const void* q, const int64_t* q_strides, const void* k,
+                           const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                           int dtype, int64_t batch, int64_t seq_len, int64_t heads,
+                           int64_t head_dim);
+
+/*
+ * Fused residual add + LayerNorm over the last dimension of contiguous rows:
+ *   residual_out   = x + update           (rounded to dtype)
+ *   normalized_out = (r - mean(r)) * rsqrt(var(r) + eps) * weight + bias
+ * with fp32 statistics. With valid_mask (one bool per row) and the
+ * B200TK_RLN_ZERO_* flags, invalid rows are zeroed in the chosen outputs.
+ * B200TK_RLN_NO_UPDATE turns the call into a plain LayerNorm of x.
+ *
+ * Replaces: transformer_opt/kernels/residual_layer_norm.py:159-238
+ * (fused_residual_layer_norm, launching _residual_layer_norm_fwd at :73-126).
+ *
+ * x, update, residual_out, normalized_out : [rows, width] contiguous.
+ * weight : [width]; bias : [width] or NULL. valid_mask : [rows] or NULL.
+ */
+B200TK_API int b200tk_residual_layer_norm_fwd(const void* x, const void* update, const void* weight,
+                                   const void* bias, const uint8_t* valid_mask,
+                                   void* residual_out, void* normalized_out, int dtype,
+                                   int64_t rows, int64_t width, float eps, uint32_t flags,
+                                   void* stream);
+
+/*
+ * Read (and, with clear != 0, reset) the device status word of `device`.
+ * Synchronises the device. Not for use inside stream capture.
+ */
+B200TK_API int b200tk_device_status(int device, uint32_t* status, int clear);
+
+/*
+ * Failure-detection self test: launches one CTA that waits on an mbarrier
+ * nothing arrives on, with a wait limit of timeout_us microseconds. The
+ * kernel gives up, records B200TK_STATUS_SELFTEST_TIMEOUT in the status word
+ * and returns; the GPU context stays usable. Synchronises the stream.
+ */
+B200TK_API int b200tk_selftest_wait_timeout(int device, uint32_t timeout_us, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200TK_H */

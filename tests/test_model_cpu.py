@@ -1,0 +1,96 @@
+"""UserOptimizedTransformer on CPU against the oracle's explicit model
+(the reference's tests/test_correctness.py strategy, :26-110)."""
+
+from __future__ import annotations
+
+import itertools
+
+import pytest
+import torch
+
+from oracle import explicit as oracle
+from tests import _golden
+from transformer_opt.submission import TransformerConfig, UserOptimizedTransformer
+
+SHAPES = [
+    (1, 32, 64, 4, 256, 2),
+    (8, 128, 256, 8, 1024, 2),
+    (2, 96, 128, 8, 512, 3),
+    (4, 64, 512, 8, 1024, 1),
+]
+
+
+def _pair(b, s, d, h, f, layers, causal, seed=0):
+    torch.manual_seed(seed)
+    baseline = oracle.BaselineTransformer(oracle.TransformerConfig(b, s, d, h, f, layers, causal)).eval()
+    optimized = UserOptimizedTransformer(TransformerConfig(b, s, d, h, f, layers, causal)).eval()
+    oracle.copy_model_weights(baseline, optimized, strict=True)
+    return baseline, optimized
+
+
+@pytest.mark.parametrize(
+    "shape,causal,padding", list(itertools.product(SHAPES, [False, True], [0.0, 0.3])), ids=str
+)
+def test_cpu_forward_matches_oracle(shape, causal, padding):
+    baseline, optimized = _pair(*shape, causal)
+    cfg = oracle.TransformerConfig(*shape, causal)
+    x, mask = oracle.generate_random_case(cfg, torch.device("cpu"), torch.float32, 7, padding)
+    with torch.inference_mode():
+        ref = baseline(x, mask)
+        opt = optimized(x, mask)
+    res = oracle.compare_outputs(ref, opt)
+    assert res.passed, res
+    assert optimized.attention_backend_counts["reference"] == shape[-1]
+
+
+def test_state_dict_is_interchangeable_both_ways():
+    baseline, optimized = _pair(2, 16, 64, 8, 128, 2, False)
+    assert list(baseline.state_dict()) == list(optimized.state_dict())
+    baseline.load_state_dict(optimized.state_dict(), strict=True)
+
+
+def test_same_seed_gives_same_initialisation():
+    cfg = (2, 16, 64, 4, 128, 2, True)
+    torch.manual_seed(123)
+    baseline = oracle.BaselineTransformer(oracle.TransformerConfig(*cfg))
+    torch.manual_seed(123)
+    optimized = UserOptimizedTransformer(TransformerConfig(*cfg))
+    for (n1, t1), (n2, t2) in zip(baseline.state_dict().items(), optimized.state_dict().items()):
+        assert n1 == n2 and torch.equal(t1, t2)
+
+
+def test_golden_model_case_through_optimized_model():
+    data = _golden.load("model.npz")
+    b, s, dm, h, f, layers, causal, seed = (int(v) for v in data["m1_cfg"])
+    torch.manual_seed(seed)
+    model = UserOptimizedTransformer(TransformerConfig(b, s, dm, h, f, layers, bool(causal))).eval()
+    x = torch.from_numpy(data["m1_x"])
+    mask = torch.from_numpy(data["m1_mask"])
+    with torch.inference_mode():
+        y = model(x, mask)
+    res = oracle.compare_outputs(torch.from_numpy(data["m1_y"]), y)
+    assert res.passed, res
+
+
+def test_explicit_all_valid_mask_matches_none():
+    _, optimized = _pair(2, 33, 64, 4, 128, 1, True)
+    x = torch.randn(2, 33, 64)
+    with torch.inference_mode():
+        a = optimized(x, None)
+        b = optimized(x, torch.ones(2, 33, dtype=torch.bool))
+    assert oracle.compare_outputs(a, b).passed
+
+
+def test_constructor_validation():
+    cfg = TransformerConfig(1, 8, 16, 2, 32, 1, False)
+    with pytest.raises(ValueError, match="attention_backend"):
+        UserOptimizedTransformer(cfg, attention_backend="mystery")
+    with pytest.raises(ValueError, match="execution_mode"):
+        UserOptimizedTransformer(cfg, execution_mode="never")
+
+
+def test_fused_route_reason_on_cpu():
+    model = UserOptimizedTransformer(TransformerConfig(1, 8, 16, 2, 32, 1, False)).eval()
+    assert model.fused_route_reason(torch.randn(1, 8, 16), None) == "CPU input"
+    sdpa = UserOptimizedTransformer(TransformerConfig(1, 8, 16, 2, 32, 1, False), "sdpa")
+    assert "explicit math" in sdpa.fused_route_reason(torch.randn(1, 8, 16), None)

@@ -1,0 +1,70 @@
+// attention.h - internal launch interfaces shared by the C ABI (capi.cu) and
+// the attention kernels. Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../../include/b200tk.h"
+
+namespace b200tk {
+
+// Arguments of the tcgen05 route. Tensor maps are built by the host (capi.cu)
+// and passed as opaque 128-byte blobs.
+struct AttnTcArgs {
+  alignas(64) unsigned char tm_q[128];
+  alignas(64) unsigned char tm_k[128];
+  alignas(64) unsigned char tm_v[128];
+  void* out;
+  const uint8_t* mask;
+  int64_t mask_sb, mask_ss;
+  int64_t batch, seq, heads, head_dim;
+  int dtype;
+  int causal;
+  float scale;
+  unsigned int* status;
+};
+
+// Keys per tile of the tcgen05 kernel for (dtype, head_dim); the query tile
+// is always 128 rows.
+int attention_tc_block_n(int dtype, int head_dim);
+cudaError_t launch_attention_tc(const AttnTcArgs& args, cudaStream_t stream);
+
+// Arguments of the CUDA-core route (any supported head_dim, any strides).
+struct AttnGenericArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  int64_t qs[3], ks[3], vs[3];  // element strides {batch, seq, head}
+  const uint8_t* mask;
+  int64_t mask_sb, mask_ss;
+  void* out;
+  int64_t batch, seq, heads, head_dim;
+  int dtype;
+  int causal;
+  float scale;
+};
+cudaError_t launch_attention_generic(const AttnGenericArgs& args, cudaStream_t stream);
+
+// Residual + LayerNorm.
+struct RlnArgs {
+  const void* x;
+  const void* update;
+  const void* weight;
+  const void* bias;
+  const uint8_t* mask;
+  void* residual_out;
+  void* normalized_out;
+  int64_t rows, width;
+  int dtype;
+  float eps;
+  uint32_t flags;
+};
+cudaError_t launch_residual_layer_norm(const RlnArgs& args, cudaStream_t stream);
+
+// Failure-detection self test (bounded wait on an mbarrier nobody completes).
+cudaError_t launch_selftest_wait_timeout(unsigned int* status, uint32_t timeout_us,
+                                         cudaStream_t stream);
+
+}  // namespace b200tk

@@ -1,0 +1,262 @@
+"""``UserOptimizedTransformer``: the inference forward on the sm_100a kernels.
+
+Drop-in for the reference's transformer_opt/submission.py:78-671 (same
+constructor ``(config, attention_backend="auto", execution_mode="auto")``,
+same ``forward(x, valid_token_mask=None)``, same counters and the same
+state-dict surface, so the organizer harness's strict ``copy_model_weights``
+works unchanged).
+
+On an sm_100 GPU in inference mode every layer runs
+  packed QKV projection (cuBLAS, fp32) or three projections (16-bit)
+  -> fused attention (libb200tk, tcgen05)  -> out_proj (cuBLAS)
+  -> fused residual + norm2 (libb200tk)    -> FFN (cuBLAS + GELU)
+  -> fused residual + next norm1 / final_norm (libb200tk)
+which is the reference's fused layer loop (:481-525) applied to every shape
+and dtype instead of four measured rows. Everything else (CPU, autograd,
+training mode, backends other than the custom one) runs the explicit
+PyTorch forward with attention through ``attention_forward``.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from transformer_opt.config import (
+    ATTENTION_BACKENDS,
+    CUSTOM_BACKEND,
+    LEGACY_CUSTOM_BACKEND,
+    MAX_NORMALIZED_WIDTH,
+    SUPPORTED_DTYPES,
+    device_supported,
+)
+from transformer_opt.dispatch import attention_forward
+from transformer_opt.kernels import _native
+from transformer_opt.kernels.residual_layer_norm import fused_residual_layer_norm, layer_norm
+from transformer_opt.model import (
+    SelfAttentionWeights,
+    TransformerConfig,
+    TransformerWeights,
+    explicit_block,
+    split_heads,
+)
+
+EXECUTION_MODES = ("auto", "eager")
+
+__all__ = ["TransformerConfig", "UserOptimizedTransformer"]
+
+
+class UserOptimizedTransformer(TransformerWeights):
+    """Transformer inference forward routed through libb200tk.so."""
+
+    def __init__(
+        self,
+        config: TransformerConfig,
+        attention_backend: str = "auto",
+        execution_mode: str = "auto",
+    ) -> None:
+        super().__init__(config)
+        if attention_backend not in ATTENTION_BACKENDS:
+            raise ValueError(
+                f"attention_backend must be one of {ATTENTION_BACKENDS}, "
+                f"got {attention_backend!r}"
+            )
+        if execution_mode not in EXECUTION_MODES:
+            raise ValueError(f"execution_mode must be one of {EXECUTION_MODES}")
+        self.attention_backend = attention_backend
+        self.execution_mode = execution_mode
+        self._lock = threading.RLock()
+        self.attention_backend_counts: Dict[str, int] = {
+            CUSTOM_BACKEND: 0,
+            "sdpa": 0,
+            "reference": 0,
+        }
+        self.fused_residual_layer_norm_calls = 0
+        self.cuda_graph_replays = 0
+        # Derived, non-persistent inference data keyed by id(attention module):
+        # (parameter signature, packed weight [3d, d], packed bias [3d]).
+        self._packed_qkv_cache: Dict[int, Tuple[tuple, torch.Tensor, torch.Tensor]] = {}
+
+    # ------------------------------------------------------------ bookkeeping
+    def reset_attention_backend_counts(self) -> None:
+        self.attention_backend_counts = {CUSTOM_BACKEND: 0, "sdpa": 0, "reference": 0}
+        self.fused_residual_layer_norm_calls = 0
+        self.cuda_graph_replays = 0
+
+    def __getstate__(self):
+        state = super().__getstate__().copy()
+        state.pop("_lock", None)
+        state["_packed_qkv_cache"] = {}
+        return state
+
+    def __setstate__(self, state):
+        super().__setstate__(state)
+        self._lock = threading.RLock()
+
+    def _apply(self, fn, recurse=True):
+        # device / dtype moves invalidate the packed projection weights
+        self._packed_qkv_cache.clear()
+        return super()._apply(fn, recurse=recurse)
+
+    # ------------------------------------------------------------ projections
+    @staticmethod
+    def _qkv_signature(attn: SelfAttentionWeights) -> tuple:
+        tensors = (
+            attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight,
+            attn.q_proj.bias, attn.k_proj.bias, attn.v_proj.bias,
+        )
+        return tuple(
+            (t.data_ptr(), t._version, t.device, t.dtype) for t in tensors if t is not None
+        )
+
+    def _project_qkv(
+        self, attn: SelfAttentionWeights, x: torch.Tensor
+    ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """q, k, v as [B, S, H, D] views (strided views of one GEMM for fp32)."""
+        batch, seq_len, _ = x.shape
+        use_packed = x.is_cuda and x.dtype == torch.float32 and not torch.is_grad_enabled()
+        if not use_packed:
+            # 16-bit: the three projections are the baseline's own GEMM calls,
+            # keeping their rounding identical to the explicit model.
+            return (
+                split_heads(attn.q_proj(x), attn.num_heads),
+                split_heads(attn.k_proj(x), attn.num_heads),
+                split_heads(attn.v_proj(x), attn.num_heads),
+            )
+        signature = self._qkv_signature(attn)
+        cached = self._packed_qkv_cache.get(id(attn))
+        if cached is None or cached[0] != signature:
+            weight = torch.cat((attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight), 0)
+            bias = torch.cat((attn.q_proj.bias, attn.k_proj.bias, attn.v_proj.bias), 0)
+            cached = (signature, weight.detach(), bias.detach())
+            self._packed_qkv_cache[id(attn)] = cached
+        projected = F.linear(x, cached[1], cached[2])
+        qkv = projected.view(batch, seq_len, 3, attn.num_heads, attn.head_dim)
+        return qkv.unbind(dim=2)
+
+    def _attention(
+        self,
+        attn: SelfAttentionWeights,
+        x: torch.Tensor,
+        valid_token_mask: Optional[torch.Tensor],
+        causal: bool,
+    ) -> torch.Tensor:
+        batch, seq_len, _ = x.shape
+        q, k, v = self._project_qkv(attn, x)
+        context, dispatch = attention_forward(
+            q, k, v, valid_token_mask, causal=causal, scale=attn.scale,
+            backend=self.attention_backend,
+        )
+        self.attention_backend_counts[dispatch.selected] += 1
+        return attn.out_proj(context.reshape(batch, seq_len, attn.d_model))
+
+    # ---------------------------------------------------------------- routing
+    def fused_route_reason(
+        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
+    ) -> Optional[str]:
+        """None when the forward runs on the fused kernels, else why not."""
+        if self.attention_backend not in ("auto", CUSTOM_BACKEND, LEGACY_CUSTOM_BACKEND):
+            return f"attention_backend={self.attention_backend!r} requests explicit math"
+        if not x.is_cuda:
+            return "CPU input"
+        reason = device_supported(x.device)
+        if reason is not None:
+            return reason
+        if x.dtype not in SUPPORTED_DTYPES:
+            return f"dtype {x.dtype} is outside the fused envelope"
+        if x.ndim != 3 or x.shape[-1] != self.config.d_model:
+            return "x must be [batch, seq, d_model]"
+        if not x.is_contiguous():
+            return "x must be contiguous"
+        if self.training or torch.is_grad_enabled():
+            return "the fused route is inference-only"
+        compiler = getattr(torch, "compiler", None)
+        if compiler is not None and compiler.is_compiling():
+            return "torch.compile tracing"
+        if self.config.d_model > MAX_NORMALIZED_WIDTH:
+            return "d_model exceeds the LayerNorm kernel limit"
+        if valid_token_mask is not None and not (
+            valid_token_mask.shape == x.shape[:2]
+            and valid_token_mask.dtype is torch.bool
+            and valid_token_mask.device == x.device
+            and valid_token_mask.is_contiguous()
+        ):
+            return "valid_token_mask must be a contiguous [batch, seq] bool tensor on x's device"
+        for module in self.modules():
+            if isinstance(module, nn.LayerNorm) and (
+                module.weight is None or module.weight.dtype != x.dtype
+            ):
+                return "LayerNorm parameters must be affine and in x's dtype"
+        return None
+
+    def forward(
+        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
+    ) -> torch.Tensor:
+        reason = self.fused_route_reason(x, valid_token_mask)
+        if reason is None:
+            _native.load()  # on an eligible GPU a missing library is an error
+            return self._forward_fused(x, valid_token_mask)
+        return self._forward_eager(x, valid_token_mask)
+
+    # ----------------------------------------------------------------- fused
+    def _fused_residual_norm(
+        self,
+        x: torch.Tensor,
+        update: torch.Tensor,
+        norm: nn.LayerNorm,
+        valid_token_mask: Optional[torch.Tensor],
+        *,
+        zero_invalid_residual: bool = False,
+        zero_invalid_normalized: bool = False,
+    ) -> Tuple[torch.Tensor, torch.Tensor]:
+        residual, normalized = fused_residual_layer_norm(
+            x, update, norm.weight, norm.bias, norm.eps, valid_token_mask,
+            zero_invalid_residual=zero_invalid_residual,
+            zero_invalid_normalized=zero_invalid_normalized,
+        )
+        self.fused_residual_layer_norm_calls += 1
+        return residual, normalized
+
+    def _forward_fused(
+        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
+    ) -> torch.Tensor:
+        causal = self.config.causal
+        first = self.layers[0].norm1
+        normalized = layer_norm(x, first.weight, first.bias, first.eps)
+        for index, layer in enumerate(self.layers):
+            attn_out = self._attention(layer.attention, normalized, valid_token_mask, causal)
+            del normalized
+            x, ffn_input = self._fused_residual_norm(x, attn_out, layer.norm2, valid_token_mask)
+            del attn_out
+            ffn_out = layer.ffn_out(F.gelu(layer.ffn_in(ffn_input), approximate="none"))
+            del ffn_input
+            is_last = index + 1 == len(self.layers)
+            next_norm = self.final_norm if is_last else self.layers[index + 1].norm1
+            # Invalid rows: the block-end masked_fill zeroes the residual
+            # stream, and the model output is zeroed after final_norm.
+            x, normalized = self._fused_residual_norm(
+                x, ffn_out, next_norm, valid_token_mask,
+                zero_invalid_residual=valid_token_mask is not None,
+                zero_invalid_normalized=is_last and valid_token_mask is not None,
+            )
+            del ffn_out
+        return normalized
+
+    # ----------------------------------------------------------------- eager
+    def _forward_eager(
+        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
+    ) -> torch.Tensor:
+        causal = self.config.causal
+        for layer in self.layers:
+            x = explicit_block(
+                layer, x, valid_token_mask, causal,
+                lambda attn, h: self._attention(attn, h, valid_token_mask, causal),
+            )
+        x = self.final_norm(x)
+        if valid_token_mask is not None:
+            x = x.masked_fill(~valid_token_mask[..., None], 0)
+        return x
