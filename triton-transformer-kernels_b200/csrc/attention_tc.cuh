@@ -129,9 +129,13 @@ struct TcLayout {
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 64 + 1024;  // + alignment slack
   // TMEM columns
-  static constexpr int kTS = 0;                                 // S buffers: 2 x BN
-  static constexpr int kTPlo = 2 * BN;                          // fp32 only: 2 x BN
-  static constexpr int kTO = kSplit ? 4 * BN : 2 * BN;          // O: D columns
+  // 16-bit: P (packed pairs) overwrites the first BN/2 columns of its S
+  // buffer. fp32: P hi and P lo get buffers of their own, so no score MMA
+  // ever writes columns a P@V MMA may still be reading.
+  static constexpr int kTS = 0;                          // S buffers: 2 x BN
+  static constexpr int kTPhi = kSplit ? 2 * BN : 0;      // fp32: P hi, 2 x BN
+  static constexpr int kTPlo = 4 * BN;                   // fp32: P lo, 2 x BN
+  static constexpr int kTO = kSplit ? 6 * BN : 2 * BN;   // O: D columns
   static constexpr int kTCols = kTO + D;
   static constexpr uint32_t kTAlloc = kTCols <= 32    ? 32
                                       : kTCols <= 64  ? 64
@@ -139,6 +143,12 @@ struct TcLayout {
                                       : kTCols <= 256 ? 256
                                                       : 512;
   static constexpr int kThreads = kSplit ? 320 : 192;
+  // V (MN-major B operand of P@V): 16-bit types use the 128-byte swizzle
+  // (8-row groups, SBO 1024 B); tf32 requires the 128B_BASE32B swizzle
+  // (32-byte chunks, 4-row groups, SBO 512 B), loaded by TMA with
+  // SWIZZLE_128B_ATOM_32B.
+  static constexpr uint32_t kVLayout = kSplit ? kLayoutSw128Base32b : kLayoutSw128;
+  static constexpr uint32_t kVSbo = kSplit ? 512 : 1024;
   static_assert(kTCols <= 512, "TMEM budget");
   static_assert(D % kAtomElems == 0, "head_dim must fill whole swizzle atoms");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
@@ -218,6 +228,17 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Tile schedule. 16-bit inputs take two passes over the key tiles: pass 1
+  // only accumulates the row max and row sum, pass 2 forms probabilities
+  // that are already normalised, rounds them to T and multiplies by V -- the
+  // explicit reference's rounding boundary (softmax in fp32, then cast, then
+  // P@V). fp32 inputs take one online pass (P keeps ~fp32 precision through
+  // the 3xTF32 split, so normalising at the end is equivalent).
+  constexpr bool kTwoPass = !kSplit;
+  const int n_s = kTwoPass ? 2 * n_kv : n_kv;  // score tiles the CTA computes
+  auto in_pass2 = [&](int g) { return !kTwoPass || g >= n_kv; };
+  auto tile_of = [&](int g) { return (kTwoPass && g >= n_kv) ? g - n_kv : g; };
+
   if (warp == 4) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -231,10 +252,11 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
 #pragma unroll
       for (int a = 0; a < L::kAtoms; ++a)
         tma_load_4d(sbase + L::kQ + a * BM * 128, &p.tm_q, bar_q_full, a * L::kAtomElems, h, q0, b);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j % KST;
-        if (j >= KST)
-          ok = mbar_wait(bar_k_empty(s), ((j / KST) - 1) & 1, abort_flag, p.status,
+      for (int g = 0; g < n_s && ok; ++g) {
+        const int j = tile_of(g);
+        const int s = g % KST;
+        if (g >= KST)
+          ok = mbar_wait(bar_k_empty(s), ((g / KST) - 1) & 1, abort_flag, p.status,
                          B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
         if (!ok) break;
         mbar_arrive_expect_tx(bar_k_full(s), L::kKVBytes);
@@ -243,6 +265,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
         for (int a = 0; a < L::kAtoms; ++a)
           tma_load_4d(kdst + a * BN * 128, &p.tm_k, bar_k_full(s), a * L::kAtomElems, h, j * BN, b);
         ++issued_k[s];
+        if (!in_pass2(g)) continue;
         const int sv = j % VST;
         if (j >= VST)
           ok = mbar_wait(bar_v_empty(sv), ((j / VST) - 1) & 1, abort_flag, p.status,
@@ -285,14 +308,14 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
                           kWaitLimitNs);
       tc_fence_after();
 
-      auto issue_s = [&](int i) -> bool {
-        const int s = i % KST;
+      auto issue_s = [&](int g) -> bool {
+        const int s = g % KST;
         const uint32_t bar_k = kSplit ? bar_k_ready(s) : bar_k_full(s);
-        if (!mbar_wait(bar_k, (i / KST) & 1, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
+        if (!mbar_wait(bar_k, (g / KST) & 1, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
                        kWaitLimitNs))
           return false;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + L::kTS + (i & 1) * BN;
+        const uint32_t d_tmem = tmem + L::kTS + (g & 1) * BN;
         const uint32_t qa = sbase + L::kQ;
         const uint32_t kb = sbase + L::kK + s * L::kKStage;
         constexpr int kSteps = D / L::kUmmaK;
@@ -308,9 +331,9 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
             const int atom = byte / 128;
             const int within = byte % 128;
             const uint64_t adesc =
-                make_sdesc_sw128(qa + a_off + atom * BM * 128 + within, 16, 1024);
+                make_sdesc(qa + a_off + atom * BM * 128 + within, 16, 1024, kLayoutSw128);
             const uint64_t bdesc =
-                make_sdesc_sw128(kb + b_off + atom * BN * 128 + within, 16, 1024);
+                make_sdesc(kb + b_off + atom * BN * 128 + within, 16, 1024, kLayoutSw128);
             if constexpr (kSplit)
               mma_ss_tf32(d_tmem, adesc, bdesc, idesc_qk, (pass > 0 || ks > 0) ? 1u : 0u);
             else
@@ -318,49 +341,53 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
           }
         }
         tc_commit(bar_k_empty(s));
-        tc_commit(bar_s_full0 + 8 * (i & 1));
+        tc_commit(bar_s_full0 + 8 * (g & 1));
         return true;
       };
 
       if (ok) ok = issue_s(0);
-      if (ok && n_kv > 1) ok = issue_s(1);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        ok = mbar_wait(bar_p_full, j & 1, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
+      if (ok && n_s > 1) ok = issue_s(1);
+      for (int g = 0; g < n_s && ok; ++g) {
+        // the softmax warps are done with S_g (and wrote P_g in pass 2)
+        ok = mbar_wait(bar_p_full, g & 1, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
                        kWaitLimitNs);
         if (!ok) break;
-        const int sv = j % VST;
-        const uint32_t bar_v = kSplit ? bar_v_ready(sv) : bar_v_full(sv);
-        ok = mbar_wait(bar_v, (j / VST) & 1, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
-                       kWaitLimitNs);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t o_tmem = tmem + L::kTO;
-        const uint32_t vbuf = sbase + L::kV + sv * L::kVStage;
-        constexpr int kSteps = BN / L::kUmmaK;
-        constexpr int kPasses = kSplit ? 3 : 1;
+        if (in_pass2(g)) {
+          const int j = tile_of(g);
+          const int sv = j % VST;
+          const uint32_t bar_v = kSplit ? bar_v_ready(sv) : bar_v_full(sv);
+          ok = mbar_wait(bar_v, (j / VST) & 1, abort_flag, p.status,
+                         B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t o_tmem = tmem + L::kTO;
+          const uint32_t vbuf = sbase + L::kV + sv * L::kVStage;
+          constexpr int kSteps = BN / L::kUmmaK;
+          constexpr int kPasses = kSplit ? 3 : 1;
 #pragma unroll
-        for (int pass = 0; pass < kPasses; ++pass) {
-          // P hi lives in the S buffer, P lo (fp32 only) in its own buffer.
-          const uint32_t p_tmem = (kSplit && pass == 0) ? tmem + L::kTPlo + (j & 1) * BN
-                                                        : tmem + L::kTS + (j & 1) * BN;
-          const uint32_t v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
+          for (int pass = 0; pass < kPasses; ++pass) {
+            const uint32_t p_tmem = !kSplit    ? tmem + L::kTS + (g & 1) * BN
+                                    : pass == 0 ? tmem + L::kTPlo + (g & 1) * BN
+                                                : tmem + L::kTPhi + (g & 1) * BN;
+            const uint32_t v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
-          for (int ks = 0; ks < kSteps; ++ks) {
-            // V is MN-major: K advances over rows (128 bytes each); LBO
-            // steps across head_dim atoms, SBO across 8-row groups.
-            const uint64_t bdesc =
-                make_sdesc_sw128(vbuf + v_off + ks * L::kUmmaK * 128, BN * 128, 1024);
-            const uint32_t a_tmem = p_tmem + ks * 8;  // 8 columns per K step
-            const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
-            if constexpr (kSplit)
-              mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
-            else
-              mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+            for (int ks = 0; ks < kSteps; ++ks) {
+              // V is MN-major: K advances over 128-byte rows; LBO steps across
+              // head_dim atoms, SBO across the swizzle's row groups.
+              const uint64_t bdesc = make_sdesc(vbuf + v_off + ks * L::kUmmaK * 128, BN * 128,
+                                                L::kVSbo, L::kVLayout);
+              const uint32_t a_tmem = p_tmem + ks * 8;  // 8 columns per K step
+              const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
+              if constexpr (kSplit)
+                mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+              else
+                mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+            }
           }
+          tc_commit(bar_v_empty(sv));
+          tc_commit(bar_pv_done);
         }
-        tc_commit(bar_v_empty(sv));
-        tc_commit(bar_pv_done);
-        if (j + 2 < n_kv) ok = issue_s(j + 2);
+        if (g + 2 < n_s) ok = issue_s(g + 2);
       }
       // make sure no MMA is still writing TMEM when the CTA tears down
       tc_commit(bar_drain);
@@ -418,13 +445,16 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
     const int warp_row0 = q0 + warp * 32;
     float m_ref = -INFINITY;  // running max, log2 units
     float l_sum = 0.f;
+    float m_fin = 0.f, inv_l = 0.f;  // two-pass: final max and 1/sum
     bool ok = true;
     const float scale = p.scale;
 
-    for (int j = 0; j < n_kv && ok; ++j) {
-      const int buf = j & 1;
+    for (int g = 0; g < n_s && ok; ++g) {
+      const int buf = g & 1;
+      const int j = tile_of(g);
+      const bool pass2 = in_pass2(g);
       // warp-uniform outcome: the tcgen05.ld/st below are warp-collective
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full0 + 8 * buf, (j >> 1) & 1, abort_flag,
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full0 + 8 * buf, (g >> 1) & 1, abort_flag,
                                              p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
                                              kWaitLimitNs));
       if (!ok) break;
@@ -481,27 +511,94 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
           s[i] = allowed ? s[i] : -INFINITY;
         }
       }
-      float mx = -INFINITY;
+
+      // pv_done is a parity barrier: it only tells the current phase from the
+      // previous one. The softmax warps therefore wait for every P@V phase in
+      // order (PV_{j-1} before storing P_j), which keeps the barrier at most one
+      // phase ahead and also orders any O rescale after the MMA that wrote O.
+      auto wait_prev_pv = [&]() -> bool {
+        if (j == 0) return true;
+        const bool done = mbar_wait(bar_pv_done, (j - 1) & 1, abort_flag, p.status,
+                                    B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+        return __all_sync(0xFFFFFFFFu, done);
+      };
+
+      if constexpr (kTwoPass) {
+        if (!pass2) {
+          // pass 1: running max and sum only
+          float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
-      const float m_tile = mx * kLog2e;  // -inf stays -inf
-      const float m_new = fmaxf(m_ref, m_tile);
-      if (j == 0) {
-        m_ref = m_new;
-      } else {
-        const bool want = m_new > m_ref + kRescaleThreshold;
-        if (__any_sync(0xFFFFFFFFu, want)) {
-          // O may still be accumulating P_{j-1} V_{j-1}: wait for it.
-          ok = mbar_wait(bar_pv_done, (j - 1) & 1, abort_flag, p.status,
-                         B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-          if (!__all_sync(0xFFFFFFFFu, ok)) {
-            ok = false;
-            break;
+          for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
+          const float m_new = fmaxf(m_ref, mx * kLog2e);
+          const float m_use = m_new == -INFINITY ? 0.f : m_new;
+          const float alpha = m_ref == -INFINITY ? 0.f : ex2_approx(m_ref - m_use);
+          float part = 0.f;
+#pragma unroll
+          for (int i = 0; i < BN; ++i) part += ex2_approx(fmaf(s[i], kLog2e, -m_use));
+          l_sum = l_sum * alpha + part;
+          m_ref = m_new;
+          if (j == n_kv - 1) {
+            m_fin = m_ref == -INFINITY ? 0.f : m_ref;
+            inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
           }
-          tc_fence_after();
-          const float alpha = (m_new > m_ref) ? ex2_approx(m_ref - m_new) : 1.f;
-          if (m_new > m_ref) m_ref = m_new;
+          tc_fence_before();
+          mbar_arrive(bar_p_full);
+          continue;
+        }
+        // pass 2: normalised probabilities, rounded to T, into TMEM
+        uint32_t pk[BN / 2];
+#pragma unroll
+        for (int i = 0; i < BN / 2; ++i) {
+          const float p0 = ex2_approx(fmaf(s[2 * i], kLog2e, -m_fin)) * inv_l;
+          const float p1 = ex2_approx(fmaf(s[2 * i + 1], kLog2e, -m_fin)) * inv_l;
+          pk[i] = pack_pair<T>(p0, p1);
+        }
+        if (!wait_prev_pv()) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_st16(tmem + lane_off + L::kTS + buf * BN + c * 16, &pk[c * 16]);
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p_full);
+      } else {
+        // one online pass (fp32 / 3xTF32)
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
+        const float m_new = fmaxf(m_ref, mx * kLog2e);  // -inf stays -inf
+        bool rescale = false;
+        float alpha = 1.f;
+        if (j == 0) {
+          m_ref = m_new;
+        } else if (__any_sync(0xFFFFFFFFu, m_new > m_ref + kRescaleThreshold)) {
+          // the running max grew by more than 2^8: move every row of this
+          // warp to its new max (rows whose max did not grow keep alpha = 1)
+          rescale = true;
+          if (m_new > m_ref) {
+            alpha = ex2_approx(m_ref - m_new);
+            m_ref = m_new;
+          }
           l_sum *= alpha;
+        }
+        const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+        uint32_t ph[BN], pl[BN];
+#pragma unroll
+        for (int i = 0; i < BN; ++i) {
+          const float pv = ex2_approx(fmaf(s[i], kLog2e, -m_use));
+          l_sum += pv;
+          const uint32_t hb = __float_as_uint(pv) & 0xFFFFE000u;
+          ph[i] = hb;
+          pl[i] = __float_as_uint(pv - __uint_as_float(hb));
+        }
+        if (!wait_prev_pv()) {
+          ok = false;
+          break;
+        }
+        if (rescale) {
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
@@ -512,43 +609,18 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
             tmem_st32(addr, o);
           }
-          tc_wait_st();
         }
-      }
-      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // probabilities, row sum, and P back into TMEM
-      if constexpr (std::is_same_v<T, float>) {
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
-          uint32_t ph[32], pl[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float pv = ex2_approx(fmaf(s[c * 32 + i], kLog2e, -m_use));
-            l_sum += pv;
-            const uint32_t hb = __float_as_uint(pv) & 0xFFFFE000u;
-            ph[i] = hb;
-            pl[i] = __float_as_uint(pv - __uint_as_float(hb));
-          }
-          tmem_st32(tmem + lane_off + L::kTS + buf * BN + c * 32, ph);
-          tmem_st32(tmem + lane_off + L::kTPlo + buf * BN + c * 32, pl);
+          tmem_st32(tmem + lane_off + L::kTPhi + buf * BN + c * 32,
+                    *reinterpret_cast<const uint32_t(*)[32]>(&ph[c * 32]));
+          tmem_st32(tmem + lane_off + L::kTPlo + buf * BN + c * 32,
+                    *reinterpret_cast<const uint32_t(*)[32]>(&pl[c * 32]));
         }
-      } else {
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2_approx(fmaf(s[c * 32 + 2 * i], kLog2e, -m_use));
-            const float p1 = ex2_approx(fmaf(s[c * 32 + 2 * i + 1], kLog2e, -m_use));
-            l_sum += p0 + p1;
-            pk[i] = pack_pair<T>(p0, p1);
-          }
-          tmem_st16(tmem + lane_off + L::kTS + buf * BN + c * 16, pk);
-        }
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p_full);
       }
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar_p_full);
     }
 
     // ------------------------------------------------------------ epilogue
@@ -559,7 +631,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
     }
     if (ok) {
       tc_fence_after();
-      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      // two-pass: O is already normalised; one pass: divide by the row sum
+      const float out_scale = kTwoPass ? 1.f : (l_sum > 0.f ? 1.f / l_sum : 0.f);
       T* out_row = reinterpret_cast<T*>(p.out) +
                    ((static_cast<int64_t>(b) * p.seq + m) * p.heads + h) * D;
       const bool row_ok = m < p.seq;
@@ -574,10 +647,10 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               float4 v;
-              v.x = l_sum > 0.f ? __uint_as_float(o[4 * i + 0]) * inv : 0.f;
-              v.y = l_sum > 0.f ? __uint_as_float(o[4 * i + 1]) * inv : 0.f;
-              v.z = l_sum > 0.f ? __uint_as_float(o[4 * i + 2]) * inv : 0.f;
-              v.w = l_sum > 0.f ? __uint_as_float(o[4 * i + 3]) * inv : 0.f;
+              v.x = __uint_as_float(o[4 * i + 0]) * out_scale;
+              v.y = __uint_as_float(o[4 * i + 1]) * out_scale;
+              v.z = __uint_as_float(o[4 * i + 2]) * out_scale;
+              v.w = __uint_as_float(o[4 * i + 3]) * out_scale;
               dst[i] = v;
             }
           } else {
@@ -587,11 +660,9 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
               uint4 v;
               uint32_t* vv = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float a = l_sum > 0.f ? __uint_as_float(o[8 * i + 2 * e]) * inv : 0.f;
-                const float bb = l_sum > 0.f ? __uint_as_float(o[8 * i + 2 * e + 1]) * inv : 0.f;
-                vv[e] = pack_pair<T>(a, bb);
-              }
+              for (int e = 0; e < 4; ++e)
+                vv[e] = pack_pair<T>(__uint_as_float(o[8 * i + 2 * e]) * out_scale,
+                                     __uint_as_float(o[8 * i + 2 * e + 1]) * out_scale);
               dst[i] = v;
             }
           }

@@ -95,7 +95,8 @@ bool tma_describable(const void* ptr, const int64_t* st, int64_t batch, int64_t 
 }
 
 int encode_map(void* out, const void* ptr, const int64_t* st, int64_t batch, int64_t seq,
-               int64_t heads, int64_t head_dim, int dtype, int box_rows) {
+               int64_t heads, int64_t head_dim, int dtype, int box_rows,
+               CUtensorMapSwizzle swizzle) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
   int rc = get_encoder(&enc);
   if (rc != B200TK_OK) return rc;
@@ -114,7 +115,7 @@ int encode_map(void* out, const void* ptr, const int64_t* st, int64_t batch, int
                            : dtype == B200TK_DTYPE_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUresult r = enc(reinterpret_cast<CUtensorMap*>(out), dt, 4, const_cast<void*>(ptr), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[96];
@@ -215,11 +216,18 @@ int b200tk_attention_fwd(const void* q, const int64_t* q_strides, const void* k,
     AttnTcArgs a;
     std::memset(&a, 0, sizeof(a));
     const int bn = attention_tc_block_n(dtype, static_cast<int>(head_dim));
-    rc = encode_map(a.tm_q, q, q_strides, batch, seq_len, heads, head_dim, dtype, 128);
+    // Q and K feed the MMA K-major (128-byte swizzle). V feeds it MN-major:
+    // 16-bit V uses the same swizzle, fp32 (tf32) V needs 32-byte swizzle atoms.
+    const CUtensorMapSwizzle v_swizzle = dtype == B200TK_DTYPE_FLOAT32
+                                             ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                             : CU_TENSOR_MAP_SWIZZLE_128B;
+    rc = encode_map(a.tm_q, q, q_strides, batch, seq_len, heads, head_dim, dtype, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == B200TK_OK)
-      rc = encode_map(a.tm_k, k, k_strides, batch, seq_len, heads, head_dim, dtype, bn);
+      rc = encode_map(a.tm_k, k, k_strides, batch, seq_len, heads, head_dim, dtype, bn,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == B200TK_OK)
-      rc = encode_map(a.tm_v, v, v_strides, batch, seq_len, heads, head_dim, dtype, bn);
+      rc = encode_map(a.tm_v, v, v_strides, batch, seq_len, heads, head_dim, dtype, bn, v_swizzle);
     if (rc != B200TK_OK) return rc;
     rc = status_address(&a.status);
     if (rc != B200TK_OK) return rc;

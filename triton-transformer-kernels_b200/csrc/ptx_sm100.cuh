@@ -176,16 +176,20 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, uint32_t a_ma
          | (a_major << 15) | (b_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle (layout code 2),
-// descriptor version 1. Swizzle atoms must start on 1024-byte boundaries.
-__device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
-                                                     uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor layouts (bits 61-63).
+constexpr uint32_t kLayoutSw128 = 2;         // 16-byte chunks, 8-row period
+constexpr uint32_t kLayoutSw128Base32b = 1;  // 32-byte chunks, 4-row period (tf32 MN-major)
+
+// Shared-memory matrix descriptor, descriptor version 1 (bits 46-47). Swizzle
+// atoms must start on 1024-byte boundaries (base offset field 0).
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                               uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }
 

@@ -104,11 +104,19 @@ class UserOptimizedTransformer(TransformerWeights):
 
     # ------------------------------------------------------------ projections
     @staticmethod
-    def _qkv_signature(attn: SelfAttentionWeights) -> tuple:
+    def _qkv_signature(attn: SelfAttentionWeights) -> Optional[tuple]:
+        """Identity of the projection parameters, or None when it cannot be tracked.
+
+        Inference tensors (parameters created under torch.inference_mode) carry
+        no version counter, so in-place updates to them would go unnoticed; the
+        packed weights are then rebuilt on every call instead of cached.
+        """
         tensors = (
             attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight,
             attn.q_proj.bias, attn.k_proj.bias, attn.v_proj.bias,
         )
+        if any(t is not None and t.is_inference() for t in tensors):
+            return None
         return tuple(
             (t.data_ptr(), t._version, t.device, t.dtype) for t in tensors if t is not None
         )
@@ -129,11 +137,12 @@ class UserOptimizedTransformer(TransformerWeights):
             )
         signature = self._qkv_signature(attn)
         cached = self._packed_qkv_cache.get(id(attn))
-        if cached is None or cached[0] != signature:
+        if signature is None or cached is None or cached[0] != signature:
             weight = torch.cat((attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight), 0)
             bias = torch.cat((attn.q_proj.bias, attn.k_proj.bias, attn.v_proj.bias), 0)
             cached = (signature, weight.detach(), bias.detach())
-            self._packed_qkv_cache[id(attn)] = cached
+            if signature is not None:
+                self._packed_qkv_cache[id(attn)] = cached
         projected = F.linear(x, cached[1], cached[2])
         qkv = projected.view(batch, seq_len, 3, attn.num_heads, attn.head_dim)
         return qkv.unbind(dim=2)
