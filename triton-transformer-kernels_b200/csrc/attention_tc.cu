@@ -1,6 +1,8 @@
 // attention_tc.cu - host-side launcher of the tcgen05 attention kernels
 // (kernel: attention_tc.cuh): fills the kernel parameter block and picks the
 // (dtype, head_dim, causal, mask) instantiation.
+#include <cmath>
+
 #include "attention_tc.cuh"
 
 namespace b200tk {
@@ -23,27 +25,29 @@ cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
   prm.batch = static_cast<int>(a.batch);
   prm.seq = static_cast<int>(a.seq);
   prm.heads = static_cast<int>(a.heads);
-  prm.n_qtiles = static_cast<int>((a.seq + tc::BM - 1) / tc::BM);
+  prm.n_qtiles = 0;  // set per tile configuration
   prm.scale = a.scale;
   prm.causal_reverse = 1;
+  // T(T(qk) * 2^k) == T(qk) * 2^k for bf16 (fp32 exponent range), so the
+  // kernel may skip the second rounding; not for fp16 (subnormals round).
+  int exponent = 0;
+  prm.scale_pow2 = a.dtype == B200TK_DTYPE_BFLOAT16 && a.scale > 0.f &&
+                   std::frexp(a.scale, &exponent) == 0.5f;
   prm.status = a.status;
-  const int64_t grid64 = static_cast<int64_t>(prm.n_qtiles) * a.batch * a.heads;
-  if (grid64 > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
-  const int grid = static_cast<int>(grid64);
   const bool causal = a.causal != 0;
   const bool has_mask = a.mask != nullptr;
   const bool d64 = a.head_dim == 64;
   if (a.head_dim != 64 && a.head_dim != 128) return cudaErrorInvalidValue;
   switch (a.dtype) {
     case B200TK_DTYPE_BFLOAT16:
-      return d64 ? tc::launch_dtype_hd<__nv_bfloat16, 64>(prm, grid, causal, has_mask, stream)
-                 : tc::launch_dtype_hd<__nv_bfloat16, 128>(prm, grid, causal, has_mask, stream);
+      return d64 ? tc::launch_dtype_hd<__nv_bfloat16, 64>(prm, causal, has_mask, stream)
+                 : tc::launch_dtype_hd<__nv_bfloat16, 128>(prm, causal, has_mask, stream);
     case B200TK_DTYPE_FLOAT16:
-      return d64 ? tc::launch_dtype_hd<__half, 64>(prm, grid, causal, has_mask, stream)
-                 : tc::launch_dtype_hd<__half, 128>(prm, grid, causal, has_mask, stream);
+      return d64 ? tc::launch_dtype_hd<__half, 64>(prm, causal, has_mask, stream)
+                 : tc::launch_dtype_hd<__half, 128>(prm, causal, has_mask, stream);
     case B200TK_DTYPE_FLOAT32:
-      return d64 ? tc::launch_dtype_hd<float, 64>(prm, grid, causal, has_mask, stream)
-                 : tc::launch_dtype_hd<float, 128>(prm, grid, causal, has_mask, stream);
+      return d64 ? tc::launch_dtype_hd<float, 64>(prm, causal, has_mask, stream)
+                 : tc::launch_dtype_hd<float, 128>(prm, causal, has_mask, stream);
     default:
       return cudaErrorInvalidValue;
   }

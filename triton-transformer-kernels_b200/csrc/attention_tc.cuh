@@ -1,26 +1,27 @@
 // attention_tc.cuh - fused attention forward on sm_100a tensor cores.
 //
-// One CTA owns a 128-row query tile of one (batch, head) and walks the key /
-// value tiles of that head with an online softmax (the algorithm of the
-// reference kernel transformer_opt/kernels/attention.py:103-265):
-//   * warp 4 (producer)  : TMA loads of Q once and of K/V tiles into
-//                          KST/VST-deep smem rings (128-byte swizzle).
-//   * warp 5 (MMA issuer): one elected thread issues tcgen05.mma:
-//                          S_j = Q K_j^T into a double-buffered TMEM score
-//                          tile, then O += P_j V_j with P read from TMEM.
-//   * warps 0-3 (softmax): thread r owns query row r (TMEM lane r). It reads
-//                          S_j with tcgen05.ld, reproduces the reference's
-//                          dtype boundaries, masks (causal diagonal, sequence
-//                          end, key padding), keeps the running max / sum in
-//                          fp32, writes P_j back into TMEM, rescales O only
-//                          when its running max grew by more than 2^8, and
-//                          finally normalises O and stores the output row.
-//   * warps 6-9 (fp32 only): split every fp32 tile in smem into a tf32 "hi"
-//                          part (in place) and the residual "lo" part, so
-//                          that each product runs as hi*hi + hi*lo + lo*hi
-//                          (3xTF32) on the tf32 tensor-core path.
-// Causal tiles beyond the diagonal are never loaded (the key loop ends at
-// min(S, q0 + 128)), matching the reference's end bound (:163-166).
+// One CTA owns NQ (1 or 2) 128-row query tiles of one (batch, head) and walks
+// the key / value tiles of that head (the algorithm of the reference kernel
+// transformer_opt/kernels/attention.py:103-265):
+//   * producer warp : TMA loads of the Q tiles once and of K/V tiles into
+//                     KST/VST-deep smem rings (128-byte swizzle), shared by
+//                     all query tiles of the CTA.
+//   * MMA warp      : one elected thread issues tcgen05.mma: S_t = Q_t K_j^T
+//                     into TMEM score buffers, then O_t += P_t V_j with P read
+//                     from TMEM. With two query tiles each has one score
+//                     buffer, so tile 0's softmax overlaps tile 1's MMAs and
+//                     vice versa; with one tile the score buffer is doubled.
+//   * softmax warps : warpgroup t (4 warps) owns query tile t; thread r owns
+//                     row r (TMEM lane r). It reads S with tcgen05.ld,
+//                     reproduces the reference's dtype boundaries, masks
+//                     (causal diagonal, sequence end, key padding), keeps the
+//                     row max / sum in fp32, writes P back into TMEM and
+//                     finally stores the normalised output row.
+//   * split warps   : (fp32 only) split every fp32 tile in smem into a tf32
+//                     "hi" part (in place) and the residual "lo" part, so each
+//                     product runs as lo*hi + hi*lo + hi*hi (3xTF32).
+// Causal key tiles beyond the CTA's last query row are never loaded (the key
+// loop ends at min(S, last row + 1)), the reference's end bound (:163-166).
 //
 // Every mbarrier wait is bounded (ptx_sm100.cuh mbar_wait): on timeout the
 // CTA raises an abort flag and a device status bit, drains its own copies and
@@ -57,6 +58,7 @@ struct __align__(64) AttnTcParams {
   int batch, seq, heads, n_qtiles;
   float scale;
   int causal_reverse;  // schedule longest causal tiles first
+  int scale_pow2;      // bf16 only: scale is an exact power of two
   unsigned int* status;
 };
 
@@ -96,6 +98,75 @@ __device__ __forceinline__ void round_pair(float& a, float& b) {
   }
 }
 
+// Row max / row sum over one score row in registers with 8 independent
+// partial results: a single accumulator would make a dependency chain as
+// long as the tile.
+template <int N>
+__device__ __forceinline__ float row_max(const float (&v)[N]) {
+  float m[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m[k] = v[k];
+#pragma unroll
+  for (int i = 8; i < N; ++i) m[i % 8] = fmaxf(m[i % 8], v[i]);
+  return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])),
+               fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+}
+
+// ---- packed pair arithmetic (sm_100 f32x2 and 16-bit x2 instructions)
+// Two fp32 lanes per instruction: c = a * b, a * b + c, a + b, element-wise,
+// each with one round-to-nearest-even rounding like the scalar forms.
+__device__ __forceinline__ void mul2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "mul.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void fma2(float& a0, float& a1, float b0, float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "mov.b64 z, {%4, %5};\n\tfma.rn.f32x2 x, x, y, z;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+
+// Round two fp32 values to T and pack them (a in the low half).
+template <typename T>
+__device__ __forceinline__ uint32_t cvt_pack2(float a, float b) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void unpack2(uint32_t u, float& a, float& b) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    a = __uint_as_float(u << 16);
+    b = __uint_as_float(u & 0xFFFF0000u);
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
+    a = f.x;
+    b = f.y;
+  }
+}
+// Element-wise max of two packed T pairs (exact).
+template <typename T>
+__device__ __forceinline__ uint32_t max_pack2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (std::is_same_v<T, __nv_bfloat16>)
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else
+    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack_pair(float a, float b) {
   if constexpr (std::is_same_v<T, __nv_bfloat16>) {
@@ -107,9 +178,10 @@ __device__ __forceinline__ uint32_t pack_pair(float a, float b) {
   }
 }
 
-template <typename T, int D, int BN, int KST, int VST>
+template <typename T, int D, int BN, int KST, int VST, int NQ>
 struct TcLayout {
   static constexpr bool kSplit = ElemTraits<T>::kSplit;
+  static constexpr int kNSB = NQ == 1 ? 2 : 1;    // score buffers per query tile
   static constexpr int kElem = sizeof(T);
   static constexpr int kAtomElems = 128 / kElem;  // elements per 128-byte row
   static constexpr int kAtoms = D / kAtomElems;   // swizzle atoms along head_dim
@@ -117,32 +189,49 @@ struct TcLayout {
   static constexpr int kQBytes = BM * D * kElem;
   static constexpr int kKVBytes = BN * D * kElem;
   static constexpr int kCopies = kSplit ? 2 : 1;  // hi (+ lo) buffers
-  // smem offsets (all multiples of 1024)
+  // smem offsets (all multiples of 1024). Every tile is stored hi then lo.
+  static constexpr int kQStage = kCopies * kQBytes;
   static constexpr int kQ = 0;
-  static constexpr int kQlo = kQ + kQBytes;
-  static constexpr int kK = kQ + kCopies * kQBytes;
-  static constexpr int kKStage = kCopies * kKVBytes;  // hi then lo
+  static constexpr int kK = kQ + NQ * kQStage;
+  static constexpr int kKStage = kCopies * kKVBytes;
   static constexpr int kV = kK + KST * kKStage;
   static constexpr int kVStage = kCopies * kKVBytes;
-  static constexpr int kBar = kV + VST * kVStage;
-  static constexpr int kNumBars = 1 + 1 + 3 * KST + 3 * VST + 2 + 1 + 1 + 1;
+  static constexpr bool kTwoPass = !kSplit;
+  // 16-bit (two-pass) rows are shared by two threads, each owning BN/2 keys;
+  // fp32 rows have one thread.
+  static constexpr int kThreadsPerRow = kTwoPass ? 2 : 1;
+  static constexpr int kSoftmaxWarpsPerTile = 4 * kThreadsPerRow;
+  static constexpr int kSoftmaxWarps = NQ * kSoftmaxWarpsPerTile;
+  static constexpr int kStats = kV + VST * kVStage;  // (max, sum) exchange, float2 per thread
+  static constexpr int kBar = kStats + NQ * kThreadsPerRow * BM * 8;
+  static constexpr int kNumBars = 2 + 3 * KST + 3 * VST + NQ * kNSB + 3 * NQ + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 64 + 1024;  // + alignment slack
-  // TMEM columns
-  // 16-bit: P (packed pairs) overwrites the first BN/2 columns of its S
-  // buffer. fp32: P hi and P lo get buffers of their own, so no score MMA
-  // ever writes columns a P@V MMA may still be reading.
-  static constexpr int kTS = 0;                          // S buffers: 2 x BN
-  static constexpr int kTPhi = kSplit ? 2 * BN : 0;      // fp32: P hi, 2 x BN
-  static constexpr int kTPlo = 4 * BN;                   // fp32: P lo, 2 x BN
-  static constexpr int kTO = kSplit ? 6 * BN : 2 * BN;   // O: D columns
-  static constexpr int kTCols = kTO + D;
+  // TMEM columns per query tile: S buffers, (fp32) P hi and P lo buffers, O.
+  // 16-bit P (packed pairs) overwrites the first BN/2 columns of its S buffer;
+  // fp32 P hi / lo have buffers of their own.
+  static constexpr int kTileCols = kNSB * BN * (kSplit ? 3 : 1) + D;
+  static constexpr int kTCols = NQ * kTileCols;
   static constexpr uint32_t kTAlloc = kTCols <= 32    ? 32
                                       : kTCols <= 64  ? 64
                                       : kTCols <= 128 ? 128
                                       : kTCols <= 256 ? 256
                                                       : 512;
-  static constexpr int kThreads = kSplit ? 320 : 192;
+  __host__ __device__ static constexpr int t_s(int t, int b) { return t * kTileCols + b * BN; }
+  __host__ __device__ static constexpr int t_phi(int t, int b) {
+    return t * kTileCols + (kNSB + b) * BN;
+  }
+  __host__ __device__ static constexpr int t_plo(int t, int b) {
+    return t * kTileCols + (2 * kNSB + b) * BN;
+  }
+  __host__ __device__ static constexpr int t_o(int t) {
+    return t * kTileCols + kNSB * BN * (kSplit ? 3 : 1);
+  }
+  // warps: [softmax][producer][MMA][fp32: split x 4]
+  static constexpr int kProducerWarp = kSoftmaxWarps;
+  static constexpr int kMmaWarp = kSoftmaxWarps + 1;
+  static constexpr int kSplitWarp0 = kSoftmaxWarps + 2;
+  static constexpr int kThreads = 32 * (kSoftmaxWarps + 2 + (kSplit ? 4 : 0));
   // V (MN-major B operand of P@V): 16-bit types use the 128-byte swizzle
   // (8-row groups, SBO 1024 B); tf32 requires the 128B_BASE32B swizzle
   // (32-byte chunks, 4-row groups, SBO 512 B), loaded by TMA with
@@ -150,15 +239,18 @@ struct TcLayout {
   static constexpr uint32_t kVLayout = kSplit ? kLayoutSw128Base32b : kLayoutSw128;
   static constexpr uint32_t kVSbo = kSplit ? 512 : 1024;
   static_assert(kTCols <= 512, "TMEM budget");
+  static_assert(kBytes <= 232448, "shared memory budget");
   static_assert(D % kAtomElems == 0, "head_dim must fill whole swizzle atoms");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(NQ == 1 || NQ == 2, "one or two query tiles per CTA");
 };
 
-template <typename T, int D, int BN, int KST, int VST, bool CAUSAL, bool HAS_MASK>
-__global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
+template <typename T, int D, int BN, int KST, int VST, int NQ, bool CAUSAL, bool HAS_MASK>
+__global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
     attention_fwd_tc_kernel(const __grid_constant__ AttnTcParams p) {
-  using L = TcLayout<T, D, BN, KST, VST>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ>;
   constexpr bool kSplit = L::kSplit;
+  constexpr int NSB = L::kNSB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -175,10 +267,12 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
   auto bar_v_full = [&](int s) { return vb + 8 * s; };
   auto bar_v_ready = [&](int s) { return vb + 8 * (VST + s); };
   auto bar_v_empty = [&](int s) { return vb + 8 * (2 * VST + s); };
-  const uint32_t bar_s_full0 = vb + 8 * 3 * VST;
-  const uint32_t bar_p_full = bar_s_full0 + 16;
-  const uint32_t bar_pv_done = bar_p_full + 8;
-  const uint32_t bar_drain = bar_pv_done + 8;
+  const uint32_t tb = vb + 8 * 3 * VST;
+  auto bar_s_full = [&](int t, int buf) { return tb + 8 * (t * NSB + buf); };
+  auto bar_p_full = [&](int t) { return tb + 8 * (NQ * NSB + t); };
+  auto bar_pv_done = [&](int t) { return tb + 8 * (NQ * NSB + NQ + t); };
+  auto bar_stats = [&](int t) { return tb + 8 * (NQ * NSB + 2 * NQ + t); };
+  const uint32_t bar_drain = tb + 8 * (NQ * NSB + 3 * NQ);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
 
@@ -194,8 +288,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
   if (CAUSAL && p.causal_reverse) qt = p.n_qtiles - 1 - qt;
   const int b = bh / p.heads;
   const int h = bh - b * p.heads;
-  const int q0 = qt * BM;
-  const int kv_end = CAUSAL ? min(p.seq, q0 + BM) : p.seq;
+  const int q0 = qt * NQ * BM;  // first query row of the CTA
+  const int kv_end = CAUSAL ? min(p.seq, q0 + NQ * BM) : p.seq;
   const int n_kv = (kv_end + BN - 1) / BN;
 
   if (tid == 0) {
@@ -211,15 +305,17 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
       mbar_init(bar_v_ready(s), 128);
       mbar_init(bar_v_empty(s), 1);
     }
-    mbar_init(bar_s_full0, 1);
-    mbar_init(bar_s_full0 + 8, 1);
-    mbar_init(bar_p_full, 128);
-    mbar_init(bar_pv_done, 1);
+    for (int t = 0; t < NQ; ++t) {
+      for (int bf = 0; bf < NSB; ++bf) mbar_init(bar_s_full(t, bf), 1);
+      mbar_init(bar_p_full(t), 128 * L::kThreadsPerRow);
+      mbar_init(bar_pv_done(t), 1);
+      mbar_init(bar_stats(t), 128 * L::kThreadsPerRow);
+    }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
-  if (warp == 5) {
+  if (warp == L::kMmaWarp) {
     tmem_alloc(smem_u32(tmem_slot), L::kTAlloc);
     tmem_relinquish();
   }
@@ -234,12 +330,14 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
   // explicit reference's rounding boundary (softmax in fp32, then cast, then
   // P@V). fp32 inputs take one online pass (P keeps ~fp32 precision through
   // the 3xTF32 split, so normalising at the end is equivalent).
-  constexpr bool kTwoPass = !kSplit;
-  const int n_s = kTwoPass ? 2 * n_kv : n_kv;  // score tiles the CTA computes
+  // With two query tiles per CTA, both tiles share every K/V tile; each has
+  // one score buffer, so one tile's softmax overlaps the other tile's MMAs.
+  constexpr bool kTwoPass = L::kTwoPass;
+  const int n_s = kTwoPass ? 2 * n_kv : n_kv;  // score tiles per query tile
   auto in_pass2 = [&](int g) { return !kTwoPass || g >= n_kv; };
   auto tile_of = [&](int g) { return (kTwoPass && g >= n_kv) ? g - n_kv : g; };
 
-  if (warp == 4) {
+  if (warp == L::kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_q);
@@ -248,10 +346,13 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
       int issued_k[KST] = {};
       int issued_v[VST] = {};
       bool ok = true;
-      mbar_arrive_expect_tx(bar_q_full, L::kQBytes);
+      mbar_arrive_expect_tx(bar_q_full, NQ * L::kQBytes);
 #pragma unroll
-      for (int a = 0; a < L::kAtoms; ++a)
-        tma_load_4d(sbase + L::kQ + a * BM * 128, &p.tm_q, bar_q_full, a * L::kAtomElems, h, q0, b);
+      for (int t = 0; t < NQ; ++t)
+#pragma unroll
+        for (int a = 0; a < L::kAtoms; ++a)
+          tma_load_4d(sbase + L::kQ + t * L::kQStage + a * BM * 128, &p.tm_q, bar_q_full,
+                      a * L::kAtomElems, h, q0 + t * BM, b);
       for (int g = 0; g < n_s && ok; ++g) {
         const int j = tile_of(g);
         const int s = g % KST;
@@ -297,7 +398,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
           }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == L::kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t kFmt = ElemTraits<T>::kFmt;
@@ -308,22 +409,26 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
                           kWaitLimitNs);
       tc_fence_after();
 
-      auto issue_s = [&](int g) -> bool {
+      // S_t(g) = Q_t K_g^T into score buffer g % NSB of query tile t. The K
+      // tile is waited for by the first query tile and released after the last.
+      auto issue_s = [&](int t, int g) -> bool {
         const int s = g % KST;
-        const uint32_t bar_k = kSplit ? bar_k_ready(s) : bar_k_full(s);
-        if (!mbar_wait(bar_k, (g / KST) & 1, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
-                       kWaitLimitNs))
-          return false;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + L::kTS + (g & 1) * BN;
-        const uint32_t qa = sbase + L::kQ;
+        if (t == 0) {
+          const uint32_t bar_k = kSplit ? bar_k_ready(s) : bar_k_full(s);
+          if (!mbar_wait(bar_k, (g / KST) & 1, abort_flag, p.status,
+                         B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs))
+            return false;
+          tc_fence_after();
+        }
+        const uint32_t d_tmem = tmem + L::t_s(t, g % NSB);
+        const uint32_t qa = sbase + L::kQ + t * L::kQStage;
         const uint32_t kb = sbase + L::kK + s * L::kKStage;
         constexpr int kSteps = D / L::kUmmaK;
         constexpr int kPasses = kSplit ? 3 : 1;
 #pragma unroll
         for (int pass = 0; pass < kPasses; ++pass) {
           // 3xTF32 order: lo*hi, hi*lo, hi*hi (small terms first)
-          const uint32_t a_off = (kSplit && pass == 0) ? L::kQlo - L::kQ : 0;
+          const uint32_t a_off = (kSplit && pass == 0) ? L::kQBytes : 0;
           const uint32_t b_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
           for (int ks = 0; ks < kSteps; ++ks) {
@@ -340,54 +445,58 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
               mma_ss_f16(d_tmem, adesc, bdesc, idesc_qk, ks > 0 ? 1u : 0u);
           }
         }
-        tc_commit(bar_k_empty(s));
-        tc_commit(bar_s_full0 + 8 * (g & 1));
+        if (t == NQ - 1) tc_commit(bar_k_empty(s));
+        tc_commit(bar_s_full(t, g % NSB));
         return true;
       };
 
-      if (ok) ok = issue_s(0);
-      if (ok && n_s > 1) ok = issue_s(1);
+      for (int g = 0; g < NSB && g < n_s && ok; ++g)
+        for (int t = 0; t < NQ && ok; ++t) ok = issue_s(t, g);
       for (int g = 0; g < n_s && ok; ++g) {
-        // the softmax warps are done with S_g (and wrote P_g in pass 2)
-        ok = mbar_wait(bar_p_full, g & 1, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
-                       kWaitLimitNs);
-        if (!ok) break;
-        if (in_pass2(g)) {
-          const int j = tile_of(g);
-          const int sv = j % VST;
-          const uint32_t bar_v = kSplit ? bar_v_ready(sv) : bar_v_full(sv);
-          ok = mbar_wait(bar_v, (j / VST) & 1, abort_flag, p.status,
+        for (int t = 0; t < NQ && ok; ++t) {
+          // the softmax warps of tile t are done with S_t(g) (and wrote P_t(g))
+          ok = mbar_wait(bar_p_full(t), g & 1, abort_flag, p.status,
                          B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
           if (!ok) break;
-          tc_fence_after();
-          const uint32_t o_tmem = tmem + L::kTO;
-          const uint32_t vbuf = sbase + L::kV + sv * L::kVStage;
-          constexpr int kSteps = BN / L::kUmmaK;
-          constexpr int kPasses = kSplit ? 3 : 1;
-#pragma unroll
-          for (int pass = 0; pass < kPasses; ++pass) {
-            const uint32_t p_tmem = !kSplit    ? tmem + L::kTS + (g & 1) * BN
-                                    : pass == 0 ? tmem + L::kTPlo + (g & 1) * BN
-                                                : tmem + L::kTPhi + (g & 1) * BN;
-            const uint32_t v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
-#pragma unroll
-            for (int ks = 0; ks < kSteps; ++ks) {
-              // V is MN-major: K advances over 128-byte rows; LBO steps across
-              // head_dim atoms, SBO across the swizzle's row groups.
-              const uint64_t bdesc = make_sdesc(vbuf + v_off + ks * L::kUmmaK * 128, BN * 128,
-                                                L::kVSbo, L::kVLayout);
-              const uint32_t a_tmem = p_tmem + ks * 8;  // 8 columns per K step
-              const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
-              if constexpr (kSplit)
-                mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
-              else
-                mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+          if (in_pass2(g)) {
+            const int j = tile_of(g);
+            const int sv = j % VST;
+            if (t == 0) {
+              const uint32_t bar_v = kSplit ? bar_v_ready(sv) : bar_v_full(sv);
+              ok = mbar_wait(bar_v, (j / VST) & 1, abort_flag, p.status,
+                             B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+              if (!ok) break;
             }
+            tc_fence_after();
+            const uint32_t o_tmem = tmem + L::t_o(t);
+            const uint32_t vbuf = sbase + L::kV + sv * L::kVStage;
+            constexpr int kSteps = BN / L::kUmmaK;
+            constexpr int kPasses = kSplit ? 3 : 1;
+#pragma unroll
+            for (int pass = 0; pass < kPasses; ++pass) {
+              const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, g % NSB)
+                                      : pass == 0 ? tmem + L::t_plo(t, g % NSB)
+                                                  : tmem + L::t_phi(t, g % NSB);
+              const uint32_t v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
+#pragma unroll
+              for (int ks = 0; ks < kSteps; ++ks) {
+                // V is MN-major: K advances over 128-byte rows; LBO steps across
+                // head_dim atoms, SBO across the swizzle's row groups.
+                const uint64_t bdesc = make_sdesc(vbuf + v_off + ks * L::kUmmaK * 128, BN * 128,
+                                                  L::kVSbo, L::kVLayout);
+                const uint32_t a_tmem = p_tmem + ks * 8;  // 8 columns per K step
+                const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
+                if constexpr (kSplit)
+                  mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+                else
+                  mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+              }
+            }
+            tc_commit(bar_pv_done(t));
+            if (t == NQ - 1) tc_commit(bar_v_empty(sv));
           }
-          tc_commit(bar_v_empty(sv));
-          tc_commit(bar_pv_done);
+          if (g + NSB < n_s) ok = issue_s(t, g + NSB);
         }
-        if (g + 2 < n_s) ok = issue_s(g + 2);
       }
       // make sure no MMA is still writing TMEM when the CTA tears down
       tc_commit(bar_drain);
@@ -395,9 +504,9 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
       while (!mbar_try_wait(bar_drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
       }
     }
-  } else if (kSplit && warp >= 6) {
+  } else if (kSplit && warp >= L::kSplitWarp0) {
     // ------------------------------------------- fp32 hi/lo split workers
-    const int t = tid - 192;  // 0..127
+    const int t = tid - 32 * L::kSplitWarp0;  // 0..127
     auto split_tile = [&](uint32_t off, int bytes) {
       float4* hi = reinterpret_cast<float4*>(smem + off);
       float4* lo = reinterpret_cast<float4*>(smem + off + bytes);
@@ -420,7 +529,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
     bool ok = mbar_wait(bar_q_full, 0, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
                         kWaitLimitNs);
     if (ok) {
-      split_tile(L::kQ, L::kQBytes);
+      for (int qt_i = 0; qt_i < NQ; ++qt_i) split_tile(L::kQ + qt_i * L::kQStage, L::kQBytes);
       mbar_arrive(bar_q_ready);
     }
     for (int j = 0; j < n_kv && ok; ++j) {
@@ -437,137 +546,281 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
       split_tile(L::kV + sv * L::kVStage, L::kKVBytes);
       mbar_arrive(bar_v_ready(sv));
     }
-  } else if (warp < 4) {
-    // ------------------------------------------------------------- softmax
-    const int r = tid;  // query row within the tile == TMEM lane
-    const int m = q0 + r;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const int warp_row0 = q0 + warp * 32;
-    float m_ref = -INFINITY;  // running max, log2 units
-    float l_sum = 0.f;
-    float m_fin = 0.f, inv_l = 0.f;  // two-pass: final max and 1/sum
-    bool ok = true;
-    const float scale = p.scale;
+  } else if (warp < L::kSoftmaxWarps) {
+    if constexpr (kTwoPass) {
+      // -------------------------------------- softmax, 16-bit (two passes)
+      // warp = 8t + 4*half + quad: query tile t, key half `half` of every
+      // score tile, TMEM lane quadrant `quad`. Two threads share a row; each
+      // keeps the max / sum of its half and the pair combines them once, at
+      // the end of pass 1.
+      constexpr int HB = BN / 2;  // key columns per thread
+      const int t = warp >> 3;
+      const int half = (warp >> 2) & 1;
+      const int quad = warp & 3;
+      const int r = quad * 32 + lane;
+      const int row0 = q0 + t * BM;
+      const int m = row0 + r;
+      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+      const int warp_row0 = row0 + quad * 32;
+      const int c0 = half * HB;  // first key column of this thread within a tile
+      float m_run = -INFINITY;   // running max of this half, log2 units
+      float l_run = 0.f;
+      float m_fin = 0.f, inv_l = 0.f;  // row max (log2 units) and 1/row sum
+      bool ok = true;
+      const float scale = p.scale;
+      const bool pow2 = p.scale_pow2 != 0;
 
-    for (int g = 0; g < n_s && ok; ++g) {
-      const int buf = g & 1;
-      const int j = tile_of(g);
-      const bool pass2 = in_pass2(g);
-      // warp-uniform outcome: the tcgen05.ld/st below are warp-collective
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full0 + 8 * buf, (g >> 1) & 1, abort_flag,
-                                             p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
-                                             kWaitLimitNs));
-      if (!ok) break;
-      tc_fence_after();
-      const int n0 = j * BN;
-      // key-padding bits for this tile: warp-cooperative load + ballot
-      uint32_t kbits[BN / 32];
-      if constexpr (HAS_MASK) {
+      for (int g = 0; g < n_s && ok; ++g) {
+        const int buf = g % NSB;
+        const int j = tile_of(g);
+        const bool pass2 = in_pass2(g);
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full(t, buf), (g / NSB) & 1, abort_flag,
+                                               p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
+                                               kWaitLimitNs));
+        if (!ok) break;
+        tc_fence_after();
+        const int n0 = j * BN + c0;  // first key of this thread's columns
+        uint32_t raw[HB];
 #pragma unroll
-        for (int w = 0; w < BN / 32; ++w) {
-          const int n = n0 + w * 32 + lane;
-          bool valid = false;
-          if (n < p.seq) valid = p.mask[b * p.mask_sb + n * p.mask_ss] != 0;
-          kbits[w] = __ballot_sync(0xFFFFFFFFu, valid);
+        for (int c = 0; c < HB / 32; ++c)
+          tmem_ld32(tmem + lane_off + L::t_s(t, buf) + c0 + c * 32,
+                    *reinterpret_cast<uint32_t(*)[32]>(&raw[c * 32]));
+        uint32_t kbits[HB / 32];
+        if constexpr (HAS_MASK) {
+#pragma unroll
+          for (int w = 0; w < HB / 32; ++w) {
+            const int n = n0 + w * 32 + lane;
+            bool valid = false;
+            if (n < p.seq) valid = p.mask[b * p.mask_sb + n * p.mask_ss] != 0;
+            kbits[w] = __ballot_sync(0xFFFFFFFFu, valid);
+          }
         }
-      }
-      float s[BN];
-      {
-        uint32_t raw[BN / 32][32];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          tmem_ld32(tmem + lane_off + L::kTS + buf * BN + c * 32, raw[c]);
         tc_wait_ld();
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[c][i]);
-      }
-      // dtype boundaries of the explicit reference: (round(round(qk) * scale))
-      if constexpr (std::is_same_v<T, float>) {
-#pragma unroll
-        for (int i = 0; i < BN; ++i) s[i] *= scale;
-      } else {
-#pragma unroll
-        for (int i = 0; i < BN; i += 2) {
-          round_pair<T>(s[i], s[i + 1]);
-          s[i] *= scale;
-          s[i + 1] *= scale;
-          round_pair<T>(s[i], s[i + 1]);
-        }
-      }
-      const bool tail = n0 + BN > p.seq;
-      const bool diag = CAUSAL && (n0 + BN - 1 > warp_row0);
-      if (HAS_MASK || tail || diag) {
-#pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          const int n = n0 + i;
-          bool allowed;
-          if constexpr (HAS_MASK)
-            allowed = (kbits[i / 32] >> (i % 32)) & 1u;
-          else
-            allowed = n < p.seq;
-          if (CAUSAL) allowed = allowed && (n <= m);
-          s[i] = allowed ? s[i] : -INFINITY;
-        }
-      }
+        const bool masked = HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
 
-      // pv_done is a parity barrier: it only tells the current phase from the
-      // previous one. The softmax warps therefore wait for every P@V phase in
-      // order (PV_{j-1} before storing P_j), which keeps the barrier at most one
-      // phase ahead and also orders any O rescale after the MMA that wrote O.
-      auto wait_prev_pv = [&]() -> bool {
-        if (j == 0) return true;
-        const bool done = mbar_wait(bar_pv_done, (j - 1) & 1, abort_flag, p.status,
-                                    B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-        return __all_sync(0xFFFFFFFFu, done);
-      };
+        // Scores with the reference's dtype boundaries, s = T(T(qk) * scale),
+        // as fp32 pairs; masked keys become -inf. `mx` = max over the half.
+        float sv[HB];
+        float mx;
+        if (!masked) {
+          uint32_t mx2 = 0xFF80FF80u;  // (-inf, -inf) in bf16; replaced below for fp16
+          if constexpr (std::is_same_v<T, __half>) mx2 = 0xFC00FC00u;
+#pragma unroll
+          for (int i = 0; i < HB; i += 2) {
+            uint32_t r1 = cvt_pack2<T>(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1]));
+            float a, c;
+            if (std::is_same_v<T, __nv_bfloat16> && pow2) {
+              // T(r1 * 2^k) == r1 * 2^k for bf16: the second rounding is exact
+              mx2 = max_pack2<T>(mx2, r1);
+              unpack2<T>(r1, a, c);
+              mul2(a, c, scale, scale);
+            } else {
+              unpack2<T>(r1, a, c);
+              mul2(a, c, scale, scale);
+              const uint32_t r2 = cvt_pack2<T>(a, c);
+              mx2 = max_pack2<T>(mx2, r2);
+              unpack2<T>(r2, a, c);
+            }
+            sv[i] = a;
+            sv[i + 1] = c;
+          }
+          float ma, mb;
+          unpack2<T>(mx2, ma, mb);
+          mx = fmaxf(ma, mb);
+          if (std::is_same_v<T, __nv_bfloat16> && pow2) mx *= scale;
+        } else {
+#pragma unroll
+          for (int i = 0; i < HB; i += 2) {
+            float a = __uint_as_float(raw[i]), c = __uint_as_float(raw[i + 1]);
+            round_pair<T>(a, c);
+            a *= scale;
+            c *= scale;
+            round_pair<T>(a, c);
+            sv[i] = a;
+            sv[i + 1] = c;
+          }
+#pragma unroll
+          for (int i = 0; i < HB; ++i) {
+            const int n = n0 + i;
+            bool allowed;
+            if constexpr (HAS_MASK)
+              allowed = (kbits[i / 32] >> (i % 32)) & 1u;
+            else
+              allowed = n < p.seq;
+            if (CAUSAL) allowed = allowed && (n <= m);
+            sv[i] = allowed ? sv[i] : -INFINITY;
+          }
+          mx = row_max(sv);
+        }
 
-      if constexpr (kTwoPass) {
         if (!pass2) {
-          // pass 1: running max and sum only
-          float mx = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
-          const float m_new = fmaxf(m_ref, mx * kLog2e);
+          // pass 1: running max and sum of this half
+          const float m_new = fmaxf(m_run, mx * kLog2e);
           const float m_use = m_new == -INFINITY ? 0.f : m_new;
-          const float alpha = m_ref == -INFINITY ? 0.f : ex2_approx(m_ref - m_use);
-          float part = 0.f;
+          const float alpha = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_use);
+          float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < BN; ++i) part += ex2_approx(fmaf(s[i], kLog2e, -m_use));
-          l_sum = l_sum * alpha + part;
-          m_ref = m_new;
+          for (int i = 0; i < HB; i += 2) {
+            float a = sv[i], c = sv[i + 1];
+            fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
+            a = ex2_approx(a);
+            c = ex2_approx(c);
+            add2(part[i % 8], part[i % 8 + 1], a, c);
+          }
+          add2(part[0], part[1], part[2], part[3]);
+          add2(part[4], part[5], part[6], part[7]);
+          add2(part[0], part[1], part[4], part[5]);
+          l_run = l_run * alpha + (part[0] + part[1]);
+          m_run = m_new;
           if (j == n_kv - 1) {
-            m_fin = m_ref == -INFINITY ? 0.f : m_ref;
-            inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
+            // combine the two halves of the row (once per CTA)
+            float2* stats = reinterpret_cast<float2*>(smem + L::kStats);
+            stats[(t * 2 + half) * BM + r] = make_float2(m_run, l_run);
+            mbar_arrive(bar_stats(t));
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_stats(t), 0, abort_flag, p.status,
+                                                   B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs));
+            if (!ok) break;
+            const float2 other = stats[(t * 2 + (half ^ 1)) * BM + r];
+            const float mm = fmaxf(m_run, other.x);
+            const float mu = mm == -INFINITY ? 0.f : mm;
+            const float la = m_run == -INFINITY ? 0.f : l_run * ex2_approx(m_run - mu);
+            const float lb = other.x == -INFINITY ? 0.f : other.y * ex2_approx(other.x - mu);
+            // same association on both threads of the row: (half 0) + (half 1)
+            const float l = half == 0 ? la + lb : lb + la;
+            m_fin = mu;
+            inv_l = l > 0.f ? 1.f / l : 0.f;
           }
           tc_fence_before();
-          mbar_arrive(bar_p_full);
+          mbar_arrive(bar_p_full(t));
           continue;
         }
+
         // pass 2: normalised probabilities, rounded to T, into TMEM
-        uint32_t pk[BN / 2];
+        uint32_t pk[HB / 2];
 #pragma unroll
-        for (int i = 0; i < BN / 2; ++i) {
-          const float p0 = ex2_approx(fmaf(s[2 * i], kLog2e, -m_fin)) * inv_l;
-          const float p1 = ex2_approx(fmaf(s[2 * i + 1], kLog2e, -m_fin)) * inv_l;
-          pk[i] = pack_pair<T>(p0, p1);
+        for (int i = 0; i < HB; i += 2) {
+          float a = sv[i], c = sv[i + 1];
+          fma2(a, c, kLog2e, kLog2e, -m_fin, -m_fin);
+          a = ex2_approx(a);
+          c = ex2_approx(c);
+          mul2(a, c, inv_l, inv_l);
+          pk[i / 2] = cvt_pack2<T>(a, c);
         }
-        if (!wait_prev_pv()) {
-          ok = false;
-          break;
+        if (j > 0) {
+          // PV_{j-1} must have read P_{j-1} (same TMEM columns) and keeps the
+          // pv_done parity barrier at most one phase ahead
+          const bool done = mbar_wait(bar_pv_done(t), (j - 1) & 1, abort_flag, p.status,
+                                      B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+          if (!__all_sync(0xFFFFFFFFu, done)) {
+            ok = false;
+            break;
+          }
         }
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          tmem_st16(tmem + lane_off + L::kTS + buf * BN + c * 16, &pk[c * 16]);
+        for (int c = 0; c < HB / 64; ++c)
+          tmem_st32(tmem + lane_off + L::t_s(t, buf) + c0 / 2 + c * 32,
+                    *reinterpret_cast<const uint32_t(*)[32]>(&pk[c * 32]));
+        if constexpr (HB % 64 != 0)
+          tmem_st16(tmem + lane_off + L::t_s(t, buf) + c0 / 2 + (HB / 64) * 32,
+                    &pk[(HB / 64) * 32]);
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(bar_p_full);
-      } else {
-        // one online pass (fp32 / 3xTF32)
-        float mx = -INFINITY;
+        mbar_arrive(bar_p_full(t));
+      }
+
+      // epilogue: this thread stores head_dim columns [half*D/2, (half+1)*D/2)
+      if (ok) {
+        ok = mbar_wait(bar_pv_done(t), (n_kv - 1) & 1, abort_flag, p.status,
+                       B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        constexpr int DH = D / 2;
+        T* out_row = reinterpret_cast<T*>(p.out) +
+                     ((static_cast<int64_t>(b) * p.seq + m) * p.heads + h) * D + half * DH;
+        const bool row_ok = m < p.seq;
+#pragma unroll 1
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_off + L::t_o(t) + half * DH + c * 32, o);
+          tc_wait_ld();
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
 #pragma unroll
-        for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = cvt_pack2<T>(__uint_as_float(o[8 * i + 0]), __uint_as_float(o[8 * i + 1]));
+              v.y = cvt_pack2<T>(__uint_as_float(o[8 * i + 2]), __uint_as_float(o[8 * i + 3]));
+              v.z = cvt_pack2<T>(__uint_as_float(o[8 * i + 4]), __uint_as_float(o[8 * i + 5]));
+              v.w = cvt_pack2<T>(__uint_as_float(o[8 * i + 6]), __uint_as_float(o[8 * i + 7]));
+              dst[i] = v;
+            }
+          }
+        }
+      }
+    } else {
+      // ------------------------------------------ softmax, fp32 (one pass)
+      const int t = warp >> 2;         // query tile of this warpgroup
+      const int quad = warp & 3;       // TMEM lane quadrant
+      const int r = quad * 32 + lane;  // query row within the tile == TMEM lane
+      const int row0 = q0 + t * BM;
+      const int m = row0 + r;
+      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+      const int warp_row0 = row0 + quad * 32;
+      float m_ref = -INFINITY;  // running max, log2 units
+      float l_sum = 0.f;
+      bool ok = true;
+      const float scale = p.scale;
+
+      for (int g = 0; g < n_s && ok; ++g) {
+        const int buf = g % NSB;
+        const int j = g;
+        // warp-uniform outcome: the tcgen05.ld/st below are warp-collective
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full(t, buf), (g / NSB) & 1, abort_flag,
+                                               p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
+                                               kWaitLimitNs));
+        if (!ok) break;
+        tc_fence_after();
+        const int n0 = j * BN;
+        uint32_t kbits[BN / 32];
+        if constexpr (HAS_MASK) {
+#pragma unroll
+          for (int w = 0; w < BN / 32; ++w) {
+            const int n = n0 + w * 32 + lane;
+            bool valid = false;
+            if (n < p.seq) valid = p.mask[b * p.mask_sb + n * p.mask_ss] != 0;
+            kbits[w] = __ballot_sync(0xFFFFFFFFu, valid);
+          }
+        }
+        float s[BN];
+        {
+          uint32_t raw[BN / 32][32];
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+            tmem_ld32(tmem + lane_off + L::t_s(t, buf) + c * 32, raw[c]);
+          tc_wait_ld();
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[c][i]) * scale;
+        }
+        const bool tail = n0 + BN > p.seq;
+        const bool diag = CAUSAL && (n0 + BN - 1 > warp_row0);
+        if (HAS_MASK || tail || diag) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) {
+            const int n = n0 + i;
+            bool allowed;
+            if constexpr (HAS_MASK)
+              allowed = (kbits[i / 32] >> (i % 32)) & 1u;
+            else
+              allowed = n < p.seq;
+            if (CAUSAL) allowed = allowed && (n <= m);
+            s[i] = allowed ? s[i] : -INFINITY;
+          }
+        }
+        const float mx = row_max(s);
         const float m_new = fmaxf(m_ref, mx * kLog2e);  // -inf stays -inf
         bool rescale = false;
         float alpha = 1.f;
@@ -585,24 +838,36 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
         }
         const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
         uint32_t ph[BN], pl[BN];
+        float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < BN; ++i) {
           const float pv = ex2_approx(fmaf(s[i], kLog2e, -m_use));
-          l_sum += pv;
+          part[i % 8] += pv;
           const uint32_t hb = __float_as_uint(pv) & 0xFFFFE000u;
           ph[i] = hb;
           pl[i] = __float_as_uint(pv - __uint_as_float(hb));
         }
-        if (!wait_prev_pv()) {
-          ok = false;
-          break;
+        l_sum += ((part[0] + part[1]) + (part[2] + part[3])) +
+                 ((part[4] + part[5]) + (part[6] + part[7]));
+        // pv_done is a parity barrier: it only tells the current phase from
+        // the previous one. Waiting for every P@V phase in order (PV_{j-1}
+        // before storing P_j) keeps it at most one phase ahead, keeps P_{j-1}
+        // alive until its MMA has read it, and orders the O rescale after the
+        // MMA that wrote O.
+        if (j > 0) {
+          const bool done = mbar_wait(bar_pv_done(t), (j - 1) & 1, abort_flag, p.status,
+                                      B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+          if (!__all_sync(0xFFFFFFFFu, done)) {
+            ok = false;
+            break;
+          }
         }
         if (rescale) {
           tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
-            const uint32_t addr = tmem + lane_off + L::kTO + c * 32;
+            const uint32_t addr = tmem + lane_off + L::t_o(t) + c * 32;
             tmem_ld32(addr, o);
             tc_wait_ld();
 #pragma unroll
@@ -612,37 +877,34 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
         }
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
-          tmem_st32(tmem + lane_off + L::kTPhi + buf * BN + c * 32,
+          tmem_st32(tmem + lane_off + L::t_phi(t, buf) + c * 32,
                     *reinterpret_cast<const uint32_t(*)[32]>(&ph[c * 32]));
-          tmem_st32(tmem + lane_off + L::kTPlo + buf * BN + c * 32,
+          tmem_st32(tmem + lane_off + L::t_plo(t, buf) + c * 32,
                     *reinterpret_cast<const uint32_t(*)[32]>(&pl[c * 32]));
         }
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(bar_p_full);
+        mbar_arrive(bar_p_full(t));
       }
-    }
 
-    // ------------------------------------------------------------ epilogue
-    if (ok) {
-      ok = mbar_wait(bar_pv_done, (n_kv - 1) & 1, abort_flag, p.status,
-                     B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-      ok = __all_sync(0xFFFFFFFFu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      // two-pass: O is already normalised; one pass: divide by the row sum
-      const float out_scale = kTwoPass ? 1.f : (l_sum > 0.f ? 1.f / l_sum : 0.f);
-      T* out_row = reinterpret_cast<T*>(p.out) +
-                   ((static_cast<int64_t>(b) * p.seq + m) * p.heads + h) * D;
-      const bool row_ok = m < p.seq;
+      // epilogue
+      if (ok) {
+        ok = mbar_wait(bar_pv_done(t), (n_kv - 1) & 1, abort_flag, p.status,
+                       B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        const float out_scale = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        float* out_row = reinterpret_cast<float*>(p.out) +
+                         ((static_cast<int64_t>(b) * p.seq + m) * p.heads + h) * D;
+        const bool row_ok = m < p.seq;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_off + L::kTO + c * 32, o);
-        tc_wait_ld();
-        if (row_ok) {
-          if constexpr (std::is_same_v<T, float>) {
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_off + L::t_o(t) + c * 32, o);
+          tc_wait_ld();
+          if (row_ok) {
             float4* dst = reinterpret_cast<float4*>(out_row + c * 32);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -651,18 +913,6 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
               v.y = __uint_as_float(o[4 * i + 1]) * out_scale;
               v.z = __uint_as_float(o[4 * i + 2]) * out_scale;
               v.w = __uint_as_float(o[4 * i + 3]) * out_scale;
-              dst[i] = v;
-            }
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v;
-              uint32_t* vv = reinterpret_cast<uint32_t*>(&v);
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                vv[e] = pack_pair<T>(__uint_as_float(o[8 * i + 2 * e]) * out_scale,
-                                     __uint_as_float(o[8 * i + 2 * e + 1]) * out_scale);
               dst[i] = v;
             }
           }
@@ -674,16 +924,16 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST>::kThreads, 1)
   // ------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == L::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, L::kTAlloc);
   }
 }
 
-template <typename T, int D, int BN, int KST, int VST, bool CAUSAL, bool HAS_MASK>
+template <typename T, int D, int BN, int KST, int VST, int NQ, bool CAUSAL, bool HAS_MASK>
 cudaError_t launch_tc(const AttnTcParams& prm, int grid, cudaStream_t stream) {
-  using L = TcLayout<T, D, BN, KST, VST>;
-  auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, CAUSAL, HAS_MASK>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ>;
+  auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, CAUSAL, HAS_MASK>;
   // at least ~116 KB so that one CTA (and one TMEM allocation) owns each SM
   const int smem = L::kBytes > 118 * 1024 ? L::kBytes : 118 * 1024;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -692,44 +942,46 @@ cudaError_t launch_tc(const AttnTcParams& prm, int grid, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-template <typename T, int D, int BN, int KST, int VST>
-cudaError_t dispatch_flags(const AttnTcParams& prm, int grid, bool causal, bool has_mask,
-                           cudaStream_t stream) {
-  if (causal)
-    return has_mask ? launch_tc<T, D, BN, KST, VST, true, true>(prm, grid, stream)
-                    : launch_tc<T, D, BN, KST, VST, true, false>(prm, grid, stream);
-  return has_mask ? launch_tc<T, D, BN, KST, VST, false, true>(prm, grid, stream)
-                  : launch_tc<T, D, BN, KST, VST, false, false>(prm, grid, stream);
-}
-
-// Tile configuration per (dtype, head_dim): keys per tile (BN) and the K / V
-// ring depths, chosen so that shared memory stays under the 227 KB opt-in
-// limit (fp32 tiles carry both the tf32 hi and lo copies).
+// Tile configuration per (dtype, head_dim): query tiles per CTA (NQ), keys
+// per tile (BN) and the K / V ring depths, chosen so that shared memory stays
+// under the 227 KB opt-in limit (fp32 tiles carry both tf32 hi and lo copies)
+// and TMEM under 512 columns.
 template <typename T, int D>
 struct TcTile {
-  static constexpr int kBN = 128, kKST = D == 64 ? 3 : 2, kVST = D == 64 ? 3 : 2;
+  static constexpr int kNQ = 2, kBN = 128, kKST = D == 64 ? 3 : 2, kVST = D == 64 ? 3 : 2;
 };
 template <>
 struct TcTile<float, 64> {
-  static constexpr int kBN = 64, kKST = 2, kVST = 2;
+  static constexpr int kNQ = 1, kBN = 64, kKST = 2, kVST = 2;
 };
 template <>
 struct TcTile<float, 128> {
-  static constexpr int kBN = 32, kKST = 2, kVST = 1;
+  static constexpr int kNQ = 1, kBN = 32, kKST = 2, kVST = 1;
 };
 
+// Fills the grid-dependent parameters and launches the instantiation for
+// (causal, mask).
 template <typename T, int D>
-cudaError_t launch_dtype_hd(const AttnTcParams& prm, int grid, bool causal, bool has_mask,
-                            cudaStream_t stream) {
+cudaError_t launch_dtype_hd(AttnTcParams prm, bool causal, bool has_mask, cudaStream_t stream) {
   using C = TcTile<T, D>;
-  return dispatch_flags<T, D, C::kBN, C::kKST, C::kVST>(prm, grid, causal, has_mask, stream);
+  const int rows_per_cta = C::kNQ * BM;
+  prm.n_qtiles = (prm.seq + rows_per_cta - 1) / rows_per_cta;
+  const int64_t grid64 = static_cast<int64_t>(prm.n_qtiles) * prm.batch * prm.heads;
+  if (grid64 > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
+  const int grid = static_cast<int>(grid64);
+  if (causal)
+    return has_mask
+               ? launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, true, true>(prm, grid, stream)
+               : launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, true, false>(prm, grid, stream);
+  return has_mask
+             ? launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, false, true>(prm, grid, stream)
+             : launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, false, false>(prm, grid, stream);
 }
 
 // Explicit instantiations live in attention_tc_inst.cu, compiled once per
 // (dtype, head_dim) so the six variants build in parallel.
-#define B200TK_TC_DECLARE(T, D)                                                              \
-  extern template cudaError_t launch_dtype_hd<T, D>(const AttnTcParams&, int, bool, bool, \
-                                                    cudaStream_t);
+#define B200TK_TC_DECLARE(T, D) \
+  extern template cudaError_t launch_dtype_hd<T, D>(AttnTcParams, bool, bool, cudaStream_t);
 B200TK_TC_DECLARE(__nv_bfloat16, 64)
 B200TK_TC_DECLARE(__nv_bfloat16, 128)
 B200TK_TC_DECLARE(__half, 64)
