@@ -188,18 +188,18 @@ struct TcLayout {
   static constexpr int kUmmaK = 32 / kElem;       // K per MMA instruction
   static constexpr int kQBytes = BM * D * kElem;
   static constexpr int kKVBytes = BN * D * kElem;
-  static constexpr int kCopies = kSplit ? 2 : 1;  // hi (+ lo) buffers
-  // smem offsets (all multiples of 1024). Every tile is stored hi then lo.
-  static constexpr int kQStage = kCopies * kQBytes;
+  static constexpr int kCopies = kSplit ? 2 : 1;  // K/V: hi (+ lo) buffers
+  // smem offsets (all multiples of 1024). K/V tiles are stored hi then lo;
+  // Q is stored once (fp32 Q hi / lo are moved into TMEM by the split warps).
+  static constexpr int kQStage = kQBytes;
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + NQ * kQStage;
   static constexpr int kKStage = kCopies * kKVBytes;
   static constexpr int kV = kK + KST * kKStage;
   static constexpr int kVStage = kCopies * kKVBytes;
   static constexpr bool kTwoPass = !kSplit;
-  // 16-bit (two-pass) rows are shared by two threads, each owning BN/2 keys;
-  // fp32 rows have one thread.
-  static constexpr int kThreadsPerRow = kTwoPass ? 2 : 1;
+  // Every score row is shared by two threads, each owning BN/2 keys.
+  static constexpr int kThreadsPerRow = 2;
   static constexpr int kSoftmaxWarpsPerTile = 4 * kThreadsPerRow;
   static constexpr int kSoftmaxWarps = NQ * kSoftmaxWarpsPerTile;
   static constexpr int kStats = kV + VST * kVStage;  // (max, sum) exchange, float2 per thread
@@ -207,10 +207,10 @@ struct TcLayout {
   static constexpr int kNumBars = 2 + 3 * KST + 3 * VST + NQ * kNSB + 3 * NQ + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 64 + 1024;  // + alignment slack
-  // TMEM columns per query tile: S buffers, (fp32) P hi and P lo buffers, O.
-  // 16-bit P (packed pairs) overwrites the first BN/2 columns of its S buffer;
-  // fp32 P hi / lo have buffers of their own.
-  static constexpr int kTileCols = kNSB * BN * (kSplit ? 3 : 1) + D;
+  // TMEM columns per query tile: S buffers, O, and for fp32 one P hi and one
+  // P lo buffer plus the Q hi / Q lo operands of the score MMA. 16-bit P
+  // (packed pairs) overwrites the first BN/2 columns of its S buffer.
+  static constexpr int kTileCols = kSplit ? kNSB * BN + 2 * BN + 3 * D : kNSB * BN + D;
   static constexpr int kTCols = NQ * kTileCols;
   static constexpr uint32_t kTAlloc = kTCols <= 32    ? 32
                                       : kTCols <= 64  ? 64
@@ -218,15 +218,15 @@ struct TcLayout {
                                       : kTCols <= 256 ? 256
                                                       : 512;
   __host__ __device__ static constexpr int t_s(int t, int b) { return t * kTileCols + b * BN; }
-  __host__ __device__ static constexpr int t_phi(int t, int b) {
-    return t * kTileCols + (kNSB + b) * BN;
-  }
-  __host__ __device__ static constexpr int t_plo(int t, int b) {
-    return t * kTileCols + (2 * kNSB + b) * BN;
+  __host__ __device__ static constexpr int t_phi(int t) { return t * kTileCols + kNSB * BN; }
+  __host__ __device__ static constexpr int t_plo(int t) {
+    return t * kTileCols + (kNSB + 1) * BN;
   }
   __host__ __device__ static constexpr int t_o(int t) {
-    return t * kTileCols + kNSB * BN * (kSplit ? 3 : 1);
+    return t * kTileCols + (kSplit ? (kNSB + 2) * BN : kNSB * BN);
   }
+  __host__ __device__ static constexpr int t_qhi(int t) { return t_o(t) + D; }
+  __host__ __device__ static constexpr int t_qlo(int t) { return t_o(t) + 2 * D; }
   // warps: [softmax][producer][MMA][fp32: split x 4]
   static constexpr int kProducerWarp = kSoftmaxWarps;
   static constexpr int kMmaWarp = kSoftmaxWarps + 1;
@@ -243,6 +243,7 @@ struct TcLayout {
   static_assert(D % kAtomElems == 0, "head_dim must fill whole swizzle atoms");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static_assert(NQ == 1 || NQ == 2, "one or two query tiles per CTA");
+  static_assert(!kSplit || NQ == 1, "fp32 keeps one query tile per CTA");
 };
 
 template <typename T, int D, int BN, int KST, int VST, int NQ, bool CAUSAL, bool HAS_MASK>
@@ -353,31 +354,52 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         for (int a = 0; a < L::kAtoms; ++a)
           tma_load_4d(sbase + L::kQ + t * L::kQStage + a * BM * 128, &p.tm_q, bar_q_full,
                       a * L::kAtomElems, h, q0 + t * BM, b);
-      for (int g = 0; g < n_s && ok; ++g) {
-        const int j = tile_of(g);
-        const int s = g % KST;
-        if (g >= KST)
-          ok = mbar_wait(bar_k_empty(s), ((g / KST) - 1) & 1, abort_flag, p.status,
-                         B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-        if (!ok) break;
-        mbar_arrive_expect_tx(bar_k_full(s), L::kKVBytes);
-        const uint32_t kdst = sbase + L::kK + s * L::kKStage;
+      // K and V rings are filled independently: the thread polls whichever
+      // slot frees first, so a full V ring never holds back K prefetch. V_j is
+      // consumed after K of its P@V tile, so V never runs ahead of that K.
+      int gk = 0, jv = 0;
+      uint64_t t_last = globaltimer_ns();
+      while ((gk < n_s || jv < n_kv) && ok) {
+        bool progress = false;
+        if (gk < n_s) {
+          const int s = gk % KST;
+          if (gk < KST || mbar_try_wait(bar_k_empty(s), ((gk / KST) - 1) & 1)) {
+            mbar_arrive_expect_tx(bar_k_full(s), L::kKVBytes);
+            const uint32_t kdst = sbase + L::kK + s * L::kKStage;
+            const int j = tile_of(gk);
 #pragma unroll
-        for (int a = 0; a < L::kAtoms; ++a)
-          tma_load_4d(kdst + a * BN * 128, &p.tm_k, bar_k_full(s), a * L::kAtomElems, h, j * BN, b);
-        ++issued_k[s];
-        if (!in_pass2(g)) continue;
-        const int sv = j % VST;
-        if (j >= VST)
-          ok = mbar_wait(bar_v_empty(sv), ((j / VST) - 1) & 1, abort_flag, p.status,
-                         B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-        if (!ok) break;
-        mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
-        const uint32_t vdst = sbase + L::kV + sv * L::kVStage;
+            for (int a = 0; a < L::kAtoms; ++a)
+              tma_load_4d(kdst + a * BN * 128, &p.tm_k, bar_k_full(s), a * L::kAtomElems, h,
+                          j * BN, b);
+            ++issued_k[s];
+            ++gk;
+            progress = true;
+          }
+        }
+        const int k_needed = kTwoPass ? n_kv + jv : jv;  // score tile that precedes PV_jv
+        if (jv < n_kv && gk > k_needed) {
+          const int sv = jv % VST;
+          if (jv < VST || mbar_try_wait(bar_v_empty(sv), ((jv / VST) - 1) & 1)) {
+            mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
+            const uint32_t vdst = sbase + L::kV + sv * L::kVStage;
 #pragma unroll
-        for (int a = 0; a < L::kAtoms; ++a)
-          tma_load_4d(vdst + a * BN * 128, &p.tm_v, bar_v_full(sv), a * L::kAtomElems, h, j * BN, b);
-        ++issued_v[sv];
+            for (int a = 0; a < L::kAtoms; ++a)
+              tma_load_4d(vdst + a * BN * 128, &p.tm_v, bar_v_full(sv), a * L::kAtomElems, h,
+                          jv * BN, b);
+            ++issued_v[sv];
+            ++jv;
+            progress = true;
+          }
+        }
+        if (progress) {
+          t_last = globaltimer_ns();
+        } else if (*abort_flag) {
+          ok = false;
+        } else if (globaltimer_ns() - t_last > kWaitLimitNs) {
+          *abort_flag = 1;
+          atomicOr(p.status, B200TK_STATUS_PIPELINE_TIMEOUT);
+          ok = false;
+        }
       }
       if (*abort_flag) {
         // drain: every copy this thread started lands before the CTA exits
@@ -427,22 +449,26 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         constexpr int kPasses = kSplit ? 3 : 1;
 #pragma unroll
         for (int pass = 0; pass < kPasses; ++pass) {
-          // 3xTF32 order: lo*hi, hi*lo, hi*hi (small terms first)
-          const uint32_t a_off = (kSplit && pass == 0) ? L::kQBytes : 0;
+          // 3xTF32 order: lo*hi, hi*lo, hi*hi (small terms first). fp32 Q
+          // comes from TMEM (hi / lo columns written by the split warps), so
+          // the only smem operand of the score MMA is K.
+          const uint32_t q_tmem = tmem + (pass == 0 ? L::t_qlo(t) : L::t_qhi(t));
           const uint32_t b_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
           for (int ks = 0; ks < kSteps; ++ks) {
             const int byte = ks * 32;
             const int atom = byte / 128;
             const int within = byte % 128;
-            const uint64_t adesc =
-                make_sdesc(qa + a_off + atom * BM * 128 + within, 16, 1024, kLayoutSw128);
             const uint64_t bdesc =
                 make_sdesc(kb + b_off + atom * BN * 128 + within, 16, 1024, kLayoutSw128);
-            if constexpr (kSplit)
-              mma_ss_tf32(d_tmem, adesc, bdesc, idesc_qk, (pass > 0 || ks > 0) ? 1u : 0u);
-            else
+            if constexpr (kSplit) {
+              mma_ts_tf32(d_tmem, q_tmem + ks * 8, bdesc, idesc_qk,
+                          (pass > 0 || ks > 0) ? 1u : 0u);
+            } else {
+              const uint64_t adesc =
+                  make_sdesc(qa + atom * BM * 128 + within, 16, 1024, kLayoutSw128);
               mma_ss_f16(d_tmem, adesc, bdesc, idesc_qk, ks > 0 ? 1u : 0u);
+            }
           }
         }
         if (t == NQ - 1) tc_commit(bar_k_empty(s));
@@ -475,8 +501,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
 #pragma unroll
             for (int pass = 0; pass < kPasses; ++pass) {
               const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, g % NSB)
-                                      : pass == 0 ? tmem + L::t_plo(t, g % NSB)
-                                                  : tmem + L::t_phi(t, g % NSB);
+                                      : pass == 0 ? tmem + L::t_plo(t)
+                                                  : tmem + L::t_phi(t);
               const uint32_t v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
               for (int ks = 0; ks < kSteps; ++ks) {
@@ -506,22 +532,20 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
     }
   } else if (kSplit && warp >= L::kSplitWarp0) {
     // ------------------------------------------- fp32 hi/lo split workers
+    // The tf32 MMA reads the top 19 bits of each fp32 operand and ignores the
+    // low 13 mantissa bits (it truncates), so an unmodified fp32 tile is its
+    // own "hi" part; only the residual lo = x - trunc_tf32(x) is written.
     const int t = tid - 32 * L::kSplitWarp0;  // 0..127
     auto split_tile = [&](uint32_t off, int bytes) {
-      float4* hi = reinterpret_cast<float4*>(smem + off);
+      const float4* hi = reinterpret_cast<const float4*>(smem + off);
       float4* lo = reinterpret_cast<float4*>(smem + off + bytes);
       for (int i = t; i < bytes / 16; i += 128) {
-        float4 x = hi[i];
-        float4 xh, xl;
-        xh.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
-        xh.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
-        xh.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
-        xh.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
-        xl.x = x.x - xh.x;
-        xl.y = x.y - xh.y;
-        xl.z = x.z - xh.z;
-        xl.w = x.w - xh.w;
-        hi[i] = xh;
+        const float4 x = hi[i];
+        float4 xl;
+        xl.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+        xl.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+        xl.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+        xl.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
         lo[i] = xl;
       }
       fence_proxy_async_smem();
@@ -529,22 +553,54 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
     bool ok = mbar_wait(bar_q_full, 0, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
                         kWaitLimitNs);
     if (ok) {
-      for (int qt_i = 0; qt_i < NQ; ++qt_i) split_tile(L::kQ + qt_i * L::kQStage, L::kQBytes);
+      // Q row r (TMEM lane r) -> hi / lo columns of the score MMA's A operand.
+      // Warp w may only touch TMEM lanes 32*(w%4)..+31, so each split warp
+      // moves the rows of its own lane quadrant.
+      const int quad = warp & 3;
+      const int r = quad * 32 + lane;
+      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+#pragma unroll 1
+      for (int a = 0; a < L::kAtoms; ++a) {
+        uint32_t qh[32], ql[32];
+        const uint8_t* row = smem + L::kQ + a * BM * 128 + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
+          const float4 x = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) * 16));
+          const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t hb = __float_as_uint(xs[e]) & 0xFFFFE000u;
+            qh[c * 4 + e] = hb;
+            ql[c * 4 + e] = __float_as_uint(xs[e] - __uint_as_float(hb));
+          }
+        }
+        tmem_st32(tmem + lane_off + L::t_qhi(0) + a * 32, qh);
+        tmem_st32(tmem + lane_off + L::t_qlo(0) + a * 32, ql);
+      }
+      tc_wait_st();
+      tc_fence_before();
       mbar_arrive(bar_q_ready);
     }
-    for (int j = 0; j < n_kv && ok; ++j) {
+    // Split in the order the MMA consumes: K_0 .. K_{NSB-1}, then V_j, K_{j+NSB}.
+    auto split_k = [&](int j) -> bool {
       const int s = j % KST;
-      ok = mbar_wait(bar_k_full(s), (j / KST) & 1, abort_flag, p.status,
-                     B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-      if (!ok) break;
+      if (!mbar_wait(bar_k_full(s), (j / KST) & 1, abort_flag, p.status,
+                     B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs))
+        return false;
       split_tile(L::kK + s * L::kKStage, L::kKVBytes);
       mbar_arrive(bar_k_ready(s));
+      return true;
+    };
+    for (int j = 0; j < NSB && j < n_kv && ok; ++j) ok = split_k(j);
+    for (int j = 0; j < n_kv && ok; ++j) {
       const int sv = j % VST;
       ok = mbar_wait(bar_v_full(sv), (j / VST) & 1, abort_flag, p.status,
                      B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
       if (!ok) break;
       split_tile(L::kV + sv * L::kVStage, L::kKVBytes);
       mbar_arrive(bar_v_ready(sv));
+      if (j + NSB < n_kv) ok = split_k(j + NSB);
     }
   } else if (warp < L::kSoftmaxWarps) {
     if constexpr (kTwoPass) {
@@ -596,6 +652,12 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           }
         }
         tc_wait_ld();
+        if (!pass2) {
+          // pass 1 keeps nothing in TMEM: the score buffer is free as soon as
+          // it has been read, so the next score tile overlaps this math.
+          tc_fence_before();
+          mbar_arrive(bar_p_full(t));
+        }
         const bool masked = HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
 
         // Scores with the reference's dtype boundaries, s = T(T(qk) * scale),
@@ -690,8 +752,6 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             m_fin = mu;
             inv_l = l > 0.f ? 1.f / l : 0.f;
           }
-          tc_fence_before();
-          mbar_arrive(bar_p_full(t));
           continue;
         }
 
@@ -761,66 +821,70 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       }
     } else {
       // ------------------------------------------ softmax, fp32 (one pass)
-      const int t = warp >> 2;         // query tile of this warpgroup
-      const int quad = warp & 3;       // TMEM lane quadrant
-      const int r = quad * 32 + lane;  // query row within the tile == TMEM lane
-      const int row0 = q0 + t * BM;
+      // warp = 4*half + quad: key half `half` of every score tile, TMEM lane
+      // quadrant `quad`. The two threads of a row exchange their tile maxima
+      // through shared memory every tile (a bounded mbarrier round), so both
+      // keep the same running max, make the same rescale decision and each
+      // rescales its half of the O row.
+      constexpr int HB = BN / 2;
+      constexpr int DH = D / 2;
+      const int half = (warp >> 2) & 1;
+      const int quad = warp & 3;
+      const int r = quad * 32 + lane;
+      const int row0 = q0;
       const int m = row0 + r;
       const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
       const int warp_row0 = row0 + quad * 32;
-      float m_ref = -INFINITY;  // running max, log2 units
-      float l_sum = 0.f;
+      const int c0 = half * HB;
+      float* xchg = reinterpret_cast<float*>(smem + L::kStats);  // [2 slots][2 halves][BM]
+      float m_ref = -INFINITY;  // running max of the row, log2 units
+      float l_sum = 0.f;        // partial sum of this half
       bool ok = true;
       const float scale = p.scale;
 
-      for (int g = 0; g < n_s && ok; ++g) {
-        const int buf = g % NSB;
-        const int j = g;
-        // warp-uniform outcome: the tcgen05.ld/st below are warp-collective
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full(t, buf), (g / NSB) & 1, abort_flag,
+      for (int j = 0; j < n_s && ok; ++j) {
+        const int buf = j % NSB;
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full(0, buf), (j / NSB) & 1, abort_flag,
                                                p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
                                                kWaitLimitNs));
         if (!ok) break;
         tc_fence_after();
-        const int n0 = j * BN;
-        uint32_t kbits[BN / 32];
-        if constexpr (HAS_MASK) {
-#pragma unroll
-          for (int w = 0; w < BN / 32; ++w) {
-            const int n = n0 + w * 32 + lane;
+        const int n0 = j * BN + c0;
+        float sv[HB];
+        {
+          uint32_t raw[HB];
+          tmem_ld_cols<HB>(tmem + lane_off + L::t_s(0, buf) + c0, raw);
+          uint32_t kbits = 0xFFFFFFFFu;
+          if constexpr (HAS_MASK) {
+            const int n = n0 + lane;
             bool valid = false;
             if (n < p.seq) valid = p.mask[b * p.mask_sb + n * p.mask_ss] != 0;
-            kbits[w] = __ballot_sync(0xFFFFFFFFu, valid);
+            kbits = __ballot_sync(0xFFFFFFFFu, valid);
           }
-        }
-        float s[BN];
-        {
-          uint32_t raw[BN / 32][32];
-#pragma unroll
-          for (int c = 0; c < BN / 32; ++c)
-            tmem_ld32(tmem + lane_off + L::t_s(t, buf) + c * 32, raw[c]);
           tc_wait_ld();
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c)
+          for (int i = 0; i < HB; ++i) sv[i] = __uint_as_float(raw[i]) * scale;
+          const bool masked =
+              HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
+          if (masked) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[c][i]) * scale;
-        }
-        const bool tail = n0 + BN > p.seq;
-        const bool diag = CAUSAL && (n0 + BN - 1 > warp_row0);
-        if (HAS_MASK || tail || diag) {
-#pragma unroll
-          for (int i = 0; i < BN; ++i) {
-            const int n = n0 + i;
-            bool allowed;
-            if constexpr (HAS_MASK)
-              allowed = (kbits[i / 32] >> (i % 32)) & 1u;
-            else
-              allowed = n < p.seq;
-            if (CAUSAL) allowed = allowed && (n <= m);
-            s[i] = allowed ? s[i] : -INFINITY;
+            for (int i = 0; i < HB; ++i) {
+              const int n = n0 + i;
+              bool allowed = HAS_MASK ? ((kbits >> i) & 1u) != 0 : n < p.seq;
+              if (CAUSAL) allowed = allowed && (n <= m);
+              sv[i] = allowed ? sv[i] : -INFINITY;
+            }
           }
         }
-        const float mx = row_max(s);
+        // row max over both halves
+        float mx = row_max(sv);
+        xchg[((j & 1) * 2 + half) * BM + r] = mx;
+        mbar_arrive(bar_stats(0));
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_stats(0), j & 1, abort_flag, p.status,
+                                               B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs));
+        if (!ok) break;
+        mx = fmaxf(mx, xchg[((j & 1) * 2 + (half ^ 1)) * BM + r]);
+
         const float m_new = fmaxf(m_ref, mx * kLog2e);  // -inf stays -inf
         bool rescale = false;
         float alpha = 1.f;
@@ -828,7 +892,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           m_ref = m_new;
         } else if (__any_sync(0xFFFFFFFFu, m_new > m_ref + kRescaleThreshold)) {
           // the running max grew by more than 2^8: move every row of this
-          // warp to its new max (rows whose max did not grow keep alpha = 1)
+          // warp to its new max (rows whose max did not grow keep alpha = 1).
+          // The partner warp sees the same maxima and decides the same way.
           rescale = true;
           if (m_new > m_ref) {
             alpha = ex2_approx(m_ref - m_new);
@@ -837,25 +902,28 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           l_sum *= alpha;
         }
         const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-        uint32_t ph[BN], pl[BN];
         float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          const float pv = ex2_approx(fmaf(s[i], kLog2e, -m_use));
-          part[i % 8] += pv;
-          const uint32_t hb = __float_as_uint(pv) & 0xFFFFE000u;
-          ph[i] = hb;
-          pl[i] = __float_as_uint(pv - __uint_as_float(hb));
+        for (int i = 0; i < HB; i += 2) {
+          float a = sv[i], c = sv[i + 1];
+          fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
+          a = ex2_approx(a);
+          c = ex2_approx(c);
+          sv[i] = a;
+          sv[i + 1] = c;
+          add2(part[i % 8], part[i % 8 + 1], a, c);
         }
-        l_sum += ((part[0] + part[1]) + (part[2] + part[3])) +
-                 ((part[4] + part[5]) + (part[6] + part[7]));
+        add2(part[0], part[1], part[2], part[3]);
+        add2(part[4], part[5], part[6], part[7]);
+        add2(part[0], part[1], part[4], part[5]);
+        l_sum += part[0] + part[1];
         // pv_done is a parity barrier: it only tells the current phase from
         // the previous one. Waiting for every P@V phase in order (PV_{j-1}
         // before storing P_j) keeps it at most one phase ahead, keeps P_{j-1}
         // alive until its MMA has read it, and orders the O rescale after the
         // MMA that wrote O.
         if (j > 0) {
-          const bool done = mbar_wait(bar_pv_done(t), (j - 1) & 1, abort_flag, p.status,
+          const bool done = mbar_wait(bar_pv_done(0), (j - 1) & 1, abort_flag, p.status,
                                       B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
           if (!__all_sync(0xFFFFFFFFu, done)) {
             ok = false;
@@ -865,9 +933,9 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         if (rescale) {
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < DH / 32; ++c) {
             uint32_t o[32];
-            const uint32_t addr = tmem + lane_off + L::t_o(t) + c * 32;
+            const uint32_t addr = tmem + lane_off + L::t_o(0) + half * DH + c * 32;
             tmem_ld32(addr, o);
             tc_wait_ld();
 #pragma unroll
@@ -875,45 +943,58 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             tmem_st32(addr, o);
           }
         }
+        {
+          // P hi keeps the tf32 bits, P lo the exact remainder
+          uint32_t ph[HB], pl[HB];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_st32(tmem + lane_off + L::t_phi(t, buf) + c * 32,
-                    *reinterpret_cast<const uint32_t(*)[32]>(&ph[c * 32]));
-          tmem_st32(tmem + lane_off + L::t_plo(t, buf) + c * 32,
-                    *reinterpret_cast<const uint32_t(*)[32]>(&pl[c * 32]));
+          for (int i = 0; i < HB; ++i) {
+            const uint32_t hb = __float_as_uint(sv[i]) & 0xFFFFE000u;
+            ph[i] = hb;
+            pl[i] = __float_as_uint(sv[i] - __uint_as_float(hb));
+          }
+          tmem_st_cols<HB>(tmem + lane_off + L::t_phi(0) + c0, ph);
+          tmem_st_cols<HB>(tmem + lane_off + L::t_plo(0) + c0, pl);
         }
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(bar_p_full(t));
+        mbar_arrive(bar_p_full(0));
       }
 
-      // epilogue
+      // epilogue: combine the two partial row sums, store this half of O
       if (ok) {
-        ok = mbar_wait(bar_pv_done(t), (n_kv - 1) & 1, abort_flag, p.status,
-                       B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-        ok = __all_sync(0xFFFFFFFFu, ok);
+        xchg[((n_s & 1) * 2 + half) * BM + r] = l_sum;
+        mbar_arrive(bar_stats(0));
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_stats(0), n_s & 1, abort_flag, p.status,
+                                               B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs));
       }
       if (ok) {
-        tc_fence_after();
-        const float out_scale = l_sum > 0.f ? 1.f / l_sum : 0.f;
-        float* out_row = reinterpret_cast<float*>(p.out) +
-                         ((static_cast<int64_t>(b) * p.seq + m) * p.heads + h) * D;
-        const bool row_ok = m < p.seq;
+        const float other = xchg[((n_s & 1) * 2 + (half ^ 1)) * BM + r];
+        const float l = half == 0 ? l_sum + other : other + l_sum;
+        ok = mbar_wait(bar_pv_done(0), (n_kv - 1) & 1, abort_flag, p.status,
+                       B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+        if (ok) {
+          tc_fence_after();
+          const float out_scale = l > 0.f ? 1.f / l : 0.f;
+          float* out_row = reinterpret_cast<float*>(p.out) +
+                           ((static_cast<int64_t>(b) * p.seq + m) * p.heads + h) * D + half * DH;
+          const bool row_ok = m < p.seq;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_off + L::t_o(t) + c * 32, o);
-          tc_wait_ld();
-          if (row_ok) {
-            float4* dst = reinterpret_cast<float4*>(out_row + c * 32);
+          for (int c = 0; c < DH / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_off + L::t_o(0) + half * DH + c * 32, o);
+            tc_wait_ld();
+            if (row_ok) {
+              float4* dst = reinterpret_cast<float4*>(out_row + c * 32);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float4 v;
-              v.x = __uint_as_float(o[4 * i + 0]) * out_scale;
-              v.y = __uint_as_float(o[4 * i + 1]) * out_scale;
-              v.z = __uint_as_float(o[4 * i + 2]) * out_scale;
-              v.w = __uint_as_float(o[4 * i + 3]) * out_scale;
-              dst[i] = v;
+              for (int i = 0; i < 8; ++i) {
+                float4 v;
+                v.x = __uint_as_float(o[4 * i + 0]) * out_scale;
+                v.y = __uint_as_float(o[4 * i + 1]) * out_scale;
+                v.z = __uint_as_float(o[4 * i + 2]) * out_scale;
+                v.w = __uint_as_float(o[4 * i + 3]) * out_scale;
+                dst[i] = v;
+              }
             }
           }
         }
@@ -952,11 +1033,11 @@ struct TcTile {
 };
 template <>
 struct TcTile<float, 64> {
-  static constexpr int kNQ = 1, kBN = 64, kKST = 2, kVST = 2;
+  static constexpr int kNQ = 1, kBN = 64, kKST = 3, kVST = 2;
 };
 template <>
 struct TcTile<float, 128> {
-  static constexpr int kNQ = 1, kBN = 32, kKST = 2, kVST = 1;
+  static constexpr int kNQ = 1, kBN = 32, kKST = 2, kVST = 2;
 };
 
 // Fills the grid-dependent parameters and launches the instantiation for
