@@ -38,16 +38,21 @@ cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
   const bool has_mask = a.mask != nullptr;
   const bool d64 = a.head_dim == 64;
   if (a.head_dim != 64 && a.head_dim != 128) return cudaErrorInvalidValue;
+  int device = 0, num_sms = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err == cudaSuccess)
+    err = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device);
+  if (err != cudaSuccess) return err;
   switch (a.dtype) {
     case B200TK_DTYPE_BFLOAT16:
-      return d64 ? tc::launch_dtype_hd<__nv_bfloat16, 64>(prm, causal, has_mask, stream)
-                 : tc::launch_dtype_hd<__nv_bfloat16, 128>(prm, causal, has_mask, stream);
+      return d64 ? tc::launch_dtype_hd<__nv_bfloat16, 64>(prm, num_sms, causal, has_mask, stream)
+                 : tc::launch_dtype_hd<__nv_bfloat16, 128>(prm, num_sms, causal, has_mask, stream);
     case B200TK_DTYPE_FLOAT16:
-      return d64 ? tc::launch_dtype_hd<__half, 64>(prm, causal, has_mask, stream)
-                 : tc::launch_dtype_hd<__half, 128>(prm, causal, has_mask, stream);
+      return d64 ? tc::launch_dtype_hd<__half, 64>(prm, num_sms, causal, has_mask, stream)
+                 : tc::launch_dtype_hd<__half, 128>(prm, num_sms, causal, has_mask, stream);
     case B200TK_DTYPE_FLOAT32:
-      return d64 ? tc::launch_dtype_hd<float, 64>(prm, causal, has_mask, stream)
-                 : tc::launch_dtype_hd<float, 128>(prm, causal, has_mask, stream);
+      return d64 ? tc::launch_dtype_hd<float, 64>(prm, num_sms, causal, has_mask, stream)
+                 : tc::launch_dtype_hd<float, 128>(prm, num_sms, causal, has_mask, stream);
     default:
       return cudaErrorInvalidValue;
   }

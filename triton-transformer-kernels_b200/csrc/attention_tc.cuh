@@ -204,7 +204,7 @@ struct TcLayout {
   static constexpr int kSoftmaxWarps = NQ * kSoftmaxWarpsPerTile;
   static constexpr int kStats = kV + VST * kVStage;  // (max, sum) exchange, float2 per thread
   static constexpr int kBar = kStats + NQ * kThreadsPerRow * BM * 8;
-  static constexpr int kNumBars = 2 + 3 * KST + 3 * VST + NQ * kNSB + 3 * NQ + 1;
+  static constexpr int kNumBars = 2 + 3 * KST + 3 * VST + NQ * kNSB + 4 * NQ + 2;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 64 + 1024;  // + alignment slack
   // TMEM columns per query tile: S buffers, O, and for fp32 one P hi and one
@@ -252,6 +252,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
   using L = TcLayout<T, D, BN, KST, VST, NQ>;
   constexpr bool kSplit = L::kSplit;
   constexpr int NSB = L::kNSB;
+  constexpr bool kTwoPass = L::kTwoPass;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -273,25 +274,15 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
   auto bar_p_full = [&](int t) { return tb + 8 * (NQ * NSB + t); };
   auto bar_pv_done = [&](int t) { return tb + 8 * (NQ * NSB + NQ + t); };
   auto bar_stats = [&](int t) { return tb + 8 * (NQ * NSB + 2 * NQ + t); };
-  const uint32_t bar_drain = tb + 8 * (NQ * NSB + 3 * NQ);
+  auto bar_o_empty = [&](int t) { return tb + 8 * (NQ * NSB + 3 * NQ + t); };
+  const uint32_t bar_q_empty = tb + 8 * (NQ * NSB + 4 * NQ);
+  const uint32_t bar_drain = bar_q_empty + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-
-  // tile scheduling: consecutive CTAs share one (batch, head) so its K/V
-  // stay hot in L2; causal tiles run longest first.
-  const int linear = blockIdx.x;
-  const int bh = linear / p.n_qtiles;
-  int qt = linear - bh * p.n_qtiles;
-  if (CAUSAL && p.causal_reverse) qt = p.n_qtiles - 1 - qt;
-  const int b = bh / p.heads;
-  const int h = bh - b * p.heads;
-  const int q0 = qt * NQ * BM;  // first query row of the CTA
-  const int kv_end = CAUSAL ? min(p.seq, q0 + NQ * BM) : p.seq;
-  const int n_kv = (kv_end + BN - 1) / BN;
 
   if (tid == 0) {
     mbar_init(bar_q_full, 1);
@@ -311,7 +302,9 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       mbar_init(bar_p_full(t), 128 * L::kThreadsPerRow);
       mbar_init(bar_pv_done(t), 1);
       mbar_init(bar_stats(t), 128 * L::kThreadsPerRow);
+      mbar_init(bar_o_empty(t), 128 * L::kThreadsPerRow);
     }
+    mbar_init(bar_q_empty, 1);
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -325,18 +318,40 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Tile schedule. 16-bit inputs take two passes over the key tiles: pass 1
-  // only accumulates the row max and row sum, pass 2 forms probabilities
-  // that are already normalised, rounds them to T and multiplies by V -- the
-  // explicit reference's rounding boundary (softmax in fp32, then cast, then
-  // P@V). fp32 inputs take one online pass (P keeps ~fp32 precision through
-  // the 3xTF32 split, so normalising at the end is equivalent).
-  // With two query tiles per CTA, both tiles share every K/V tile; each has
-  // one score buffer, so one tile's softmax overlaps the other tile's MMAs.
-  constexpr bool kTwoPass = L::kTwoPass;
-  const int n_s = kTwoPass ? 2 * n_kv : n_kv;  // score tiles per query tile
-  auto in_pass2 = [&](int g) { return !kTwoPass || g >= n_kv; };
-  auto tile_of = [&](int g) { return (kTwoPass && g >= n_kv) ? g - n_kv : g; };
+  // Persistent schedule: CTA c processes work items c, c + gridDim.x, ...
+  // An item is NQ query tiles of one (batch, head). Items of one batch-head
+  // are adjacent (its K/V stay hot in L2) and, causally, longest first. Every
+  // role walks the same item sequence, so mbarrier phases simply continue
+  // from item to item: each role keeps running counts of the K tiles, V tiles
+  // and items it has seen.
+  //
+  // 16-bit inputs take two passes over the key tiles: pass 1 only
+  // accumulates the row max and row sum, pass 2 forms probabilities that are
+  // already normalised, rounds them to T and multiplies by V -- the explicit
+  // reference's rounding boundary (softmax in fp32, then cast, then P@V).
+  // fp32 inputs take one online pass (P keeps ~fp32 precision through the
+  // 3xTF32 split, so normalising at the end is equivalent).
+  const int total_items = p.n_qtiles * p.batch * p.heads;
+  struct Item {
+    int b, h, q0, n_kv, n_s;
+  };
+  auto item_at = [&](int it) {
+    Item w;
+    const int bh = it / p.n_qtiles;
+    int qt = it - bh * p.n_qtiles;
+    if (CAUSAL && p.causal_reverse) qt = p.n_qtiles - 1 - qt;
+    w.b = bh / p.heads;
+    w.h = bh - w.b * p.heads;
+    w.q0 = qt * NQ * BM;
+    const int kv_end = CAUSAL ? min(p.seq, w.q0 + NQ * BM) : p.seq;
+    w.n_kv = (kv_end + BN - 1) / BN;
+    w.n_s = kTwoPass ? 2 * w.n_kv : w.n_kv;
+    return w;
+  };
+  auto wait = [&](uint32_t bar, uint32_t parity) {
+    return mbar_wait(bar, parity, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
+                     kWaitLimitNs);
+  };
 
   if (warp == L::kProducerWarp) {
     // ------------------------------------------------------------ producer
@@ -347,63 +362,84 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       int issued_k[KST] = {};
       int issued_v[VST] = {};
       bool ok = true;
-      mbar_arrive_expect_tx(bar_q_full, NQ * L::kQBytes);
+      int kc = 0, vc = 0, items_loaded = 0;
+      for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+        const Item w = item_at(it);
+        auto tile_of = [&](int g) { return (kTwoPass && g >= w.n_kv) ? g - w.n_kv : g; };
+        // Q smem (and, for fp32, the Q operand in TMEM) is free once every
+        // score MMA of the previous item has completed.
+        if (k > 0 && !wait(bar_q_empty, (k - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(bar_q_full, NQ * L::kQBytes);
 #pragma unroll
-      for (int t = 0; t < NQ; ++t)
+        for (int t = 0; t < NQ; ++t)
 #pragma unroll
-        for (int a = 0; a < L::kAtoms; ++a)
-          tma_load_4d(sbase + L::kQ + t * L::kQStage + a * BM * 128, &p.tm_q, bar_q_full,
-                      a * L::kAtomElems, h, q0 + t * BM, b);
-      // K and V rings are filled independently: the thread polls whichever
-      // slot frees first, so a full V ring never holds back K prefetch. V_j is
-      // consumed after K of its P@V tile, so V never runs ahead of that K.
-      int gk = 0, jv = 0;
-      uint64_t t_last = globaltimer_ns();
-      while ((gk < n_s || jv < n_kv) && ok) {
-        bool progress = false;
-        if (gk < n_s) {
-          const int s = gk % KST;
-          if (gk < KST || mbar_try_wait(bar_k_empty(s), ((gk / KST) - 1) & 1)) {
-            mbar_arrive_expect_tx(bar_k_full(s), L::kKVBytes);
-            const uint32_t kdst = sbase + L::kK + s * L::kKStage;
-            const int j = tile_of(gk);
+          for (int a = 0; a < L::kAtoms; ++a)
+            tma_load_4d(sbase + L::kQ + t * L::kQStage + a * BM * 128, &p.tm_q, bar_q_full,
+                        a * L::kAtomElems, w.h, w.q0 + t * BM, w.b);
+        ++items_loaded;
+        // K and V rings are filled independently: the thread polls whichever
+        // slot frees first, so a full V ring never holds back K prefetch. V_j
+        // is consumed after K of its P@V tile, so V never runs ahead of it.
+        int gk = 0, jv = 0;
+        uint64_t t_last = globaltimer_ns();
+        while ((gk < w.n_s || jv < w.n_kv) && ok) {
+          bool progress = false;
+          if (gk < w.n_s) {
+            const int kg = kc + gk;
+            const int s = kg % KST;
+            if (kg < KST || mbar_try_wait(bar_k_empty(s), ((kg / KST) - 1) & 1)) {
+              mbar_arrive_expect_tx(bar_k_full(s), L::kKVBytes);
+              const uint32_t kdst = sbase + L::kK + s * L::kKStage;
+              const int j = tile_of(gk);
 #pragma unroll
-            for (int a = 0; a < L::kAtoms; ++a)
-              tma_load_4d(kdst + a * BN * 128, &p.tm_k, bar_k_full(s), a * L::kAtomElems, h,
-                          j * BN, b);
-            ++issued_k[s];
-            ++gk;
-            progress = true;
+              for (int a = 0; a < L::kAtoms; ++a)
+                tma_load_4d(kdst + a * BN * 128, &p.tm_k, bar_k_full(s), a * L::kAtomElems, w.h,
+                            j * BN, w.b);
+              ++issued_k[s];
+              ++gk;
+              progress = true;
+            }
+          }
+          const int k_needed = kTwoPass ? w.n_kv + jv : jv;  // score tile preceding PV_jv
+          if (jv < w.n_kv && gk > k_needed) {
+            const int vg = vc + jv;
+            const int sv = vg % VST;
+            if (vg < VST || mbar_try_wait(bar_v_empty(sv), ((vg / VST) - 1) & 1)) {
+              mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
+              const uint32_t vdst = sbase + L::kV + sv * L::kVStage;
+#pragma unroll
+              for (int a = 0; a < L::kAtoms; ++a)
+                tma_load_4d(vdst + a * BN * 128, &p.tm_v, bar_v_full(sv), a * L::kAtomElems, w.h,
+                            jv * BN, w.b);
+              ++issued_v[sv];
+              ++jv;
+              progress = true;
+            }
+          }
+          if (progress) {
+            t_last = globaltimer_ns();
+          } else if (*abort_flag) {
+            ok = false;
+          } else if (globaltimer_ns() - t_last > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicOr(p.status, B200TK_STATUS_PIPELINE_TIMEOUT);
+            ok = false;
           }
         }
-        const int k_needed = kTwoPass ? n_kv + jv : jv;  // score tile that precedes PV_jv
-        if (jv < n_kv && gk > k_needed) {
-          const int sv = jv % VST;
-          if (jv < VST || mbar_try_wait(bar_v_empty(sv), ((jv / VST) - 1) & 1)) {
-            mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
-            const uint32_t vdst = sbase + L::kV + sv * L::kVStage;
-#pragma unroll
-            for (int a = 0; a < L::kAtoms; ++a)
-              tma_load_4d(vdst + a * BN * 128, &p.tm_v, bar_v_full(sv), a * L::kAtomElems, h,
-                          jv * BN, b);
-            ++issued_v[sv];
-            ++jv;
-            progress = true;
-          }
-        }
-        if (progress) {
-          t_last = globaltimer_ns();
-        } else if (*abort_flag) {
-          ok = false;
-        } else if (globaltimer_ns() - t_last > kWaitLimitNs) {
-          *abort_flag = 1;
-          atomicOr(p.status, B200TK_STATUS_PIPELINE_TIMEOUT);
-          ok = false;
-        }
+        kc += w.n_s;
+        vc += w.n_kv;
       }
       if (*abort_flag) {
         // drain: every copy this thread started lands before the CTA exits
-        mbar_wait(bar_q_full, 0, abort_flag, nullptr, 0, kWaitLimitNs);
+        if (items_loaded > 0) {
+          const uint32_t par = (items_loaded - 1) & 1;
+          uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(bar_q_full, par) && globaltimer_ns() - t0 < kWaitLimitNs) {
+          }
+        }
         for (int s = 0; s < KST; ++s)
           if (issued_k[s] > 0) {
             const uint32_t par = (issued_k[s] - 1) & 1;
@@ -426,103 +462,117 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       constexpr uint32_t kFmt = ElemTraits<T>::kFmt;
       constexpr uint32_t idesc_qk = make_idesc(kFmt, 0, 0, BN, BM);  // Q K-major, K K-major
       constexpr uint32_t idesc_pv = make_idesc(kFmt, 0, 1, D, BM);   // P (tmem), V MN-major
-      const uint32_t bar_q = kSplit ? bar_q_ready : bar_q_full;
-      bool ok = mbar_wait(bar_q, 0, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
-                          kWaitLimitNs);
-      tc_fence_after();
+      bool ok = true;
+      int kc = 0, vc = 0;
+      for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+        const Item w = item_at(it);
+        auto in_pass2 = [&](int g) { return !kTwoPass || g >= w.n_kv; };
+        auto tile_of = [&](int g) { return (kTwoPass && g >= w.n_kv) ? g - w.n_kv : g; };
+        ok = wait(kSplit ? bar_q_ready : bar_q_full, k & 1);
+        if (!ok) break;
+        tc_fence_after();
 
-      // S_t(g) = Q_t K_g^T into score buffer g % NSB of query tile t. The K
-      // tile is waited for by the first query tile and released after the last.
-      auto issue_s = [&](int t, int g) -> bool {
-        const int s = g % KST;
-        if (t == 0) {
-          const uint32_t bar_k = kSplit ? bar_k_ready(s) : bar_k_full(s);
-          if (!mbar_wait(bar_k, (g / KST) & 1, abort_flag, p.status,
-                         B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs))
-            return false;
-          tc_fence_after();
-        }
-        const uint32_t d_tmem = tmem + L::t_s(t, g % NSB);
-        const uint32_t qa = sbase + L::kQ + t * L::kQStage;
-        const uint32_t kb = sbase + L::kK + s * L::kKStage;
-        constexpr int kSteps = D / L::kUmmaK;
-        constexpr int kPasses = kSplit ? 3 : 1;
-#pragma unroll
-        for (int pass = 0; pass < kPasses; ++pass) {
-          // 3xTF32 order: lo*hi, hi*lo, hi*hi (small terms first). fp32 Q
-          // comes from TMEM (hi / lo columns written by the split warps), so
-          // the only smem operand of the score MMA is K.
-          const uint32_t q_tmem = tmem + (pass == 0 ? L::t_qlo(t) : L::t_qhi(t));
-          const uint32_t b_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
-#pragma unroll
-          for (int ks = 0; ks < kSteps; ++ks) {
-            const int byte = ks * 32;
-            const int atom = byte / 128;
-            const int within = byte % 128;
-            const uint64_t bdesc =
-                make_sdesc(kb + b_off + atom * BN * 128 + within, 16, 1024, kLayoutSw128);
-            if constexpr (kSplit) {
-              mma_ts_tf32(d_tmem, q_tmem + ks * 8, bdesc, idesc_qk,
-                          (pass > 0 || ks > 0) ? 1u : 0u);
-            } else {
-              const uint64_t adesc =
-                  make_sdesc(qa + atom * BM * 128 + within, 16, 1024, kLayoutSw128);
-              mma_ss_f16(d_tmem, adesc, bdesc, idesc_qk, ks > 0 ? 1u : 0u);
-            }
-          }
-        }
-        if (t == NQ - 1) tc_commit(bar_k_empty(s));
-        tc_commit(bar_s_full(t, g % NSB));
-        return true;
-      };
-
-      for (int g = 0; g < NSB && g < n_s && ok; ++g)
-        for (int t = 0; t < NQ && ok; ++t) ok = issue_s(t, g);
-      for (int g = 0; g < n_s && ok; ++g) {
-        for (int t = 0; t < NQ && ok; ++t) {
-          // the softmax warps of tile t are done with S_t(g) (and wrote P_t(g))
-          ok = mbar_wait(bar_p_full(t), g & 1, abort_flag, p.status,
-                         B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-          if (!ok) break;
-          if (in_pass2(g)) {
-            const int j = tile_of(g);
-            const int sv = j % VST;
-            if (t == 0) {
-              const uint32_t bar_v = kSplit ? bar_v_ready(sv) : bar_v_full(sv);
-              ok = mbar_wait(bar_v, (j / VST) & 1, abort_flag, p.status,
-                             B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-              if (!ok) break;
-            }
+        // S_t(g) = Q_t K_g^T into score buffer (kc + g) % NSB of query tile
+        // t. The K tile is waited for by the first query tile and released
+        // after the last; after the item's last score MMA, Q is released.
+        auto issue_s = [&](int t, int g) -> bool {
+          const int kg = kc + g;
+          const int s = kg % KST;
+          if (t == 0) {
+            if (!wait(kSplit ? bar_k_ready(s) : bar_k_full(s), (kg / KST) & 1)) return false;
             tc_fence_after();
-            const uint32_t o_tmem = tmem + L::t_o(t);
-            const uint32_t vbuf = sbase + L::kV + sv * L::kVStage;
-            constexpr int kSteps = BN / L::kUmmaK;
-            constexpr int kPasses = kSplit ? 3 : 1;
+          }
+          const uint32_t d_tmem = tmem + L::t_s(t, kg % NSB);
+          const uint32_t qa = sbase + L::kQ + t * L::kQStage;
+          const uint32_t kb = sbase + L::kK + s * L::kKStage;
+          constexpr int kSteps = D / L::kUmmaK;
+          constexpr int kPasses = kSplit ? 3 : 1;
 #pragma unroll
-            for (int pass = 0; pass < kPasses; ++pass) {
-              const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, g % NSB)
-                                      : pass == 0 ? tmem + L::t_plo(t)
-                                                  : tmem + L::t_phi(t);
-              const uint32_t v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
+          for (int pass = 0; pass < kPasses; ++pass) {
+            // 3xTF32 order: lo*hi, hi*lo, hi*hi (small terms first). fp32 Q
+            // comes from TMEM (hi / lo columns written by the split warps),
+            // so the only smem operand of the score MMA is K.
+            const uint32_t q_tmem = tmem + (pass == 0 ? L::t_qlo(t) : L::t_qhi(t));
+            const uint32_t b_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
-              for (int ks = 0; ks < kSteps; ++ks) {
-                // V is MN-major: K advances over 128-byte rows; LBO steps across
-                // head_dim atoms, SBO across the swizzle's row groups.
-                const uint64_t bdesc = make_sdesc(vbuf + v_off + ks * L::kUmmaK * 128, BN * 128,
-                                                  L::kVSbo, L::kVLayout);
-                const uint32_t a_tmem = p_tmem + ks * 8;  // 8 columns per K step
-                const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
-                if constexpr (kSplit)
-                  mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
-                else
-                  mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+            for (int ks = 0; ks < kSteps; ++ks) {
+              const int byte = ks * 32;
+              const int atom = byte / 128;
+              const int within = byte % 128;
+              const uint64_t bdesc =
+                  make_sdesc(kb + b_off + atom * BN * 128 + within, 16, 1024, kLayoutSw128);
+              if constexpr (kSplit) {
+                mma_ts_tf32(d_tmem, q_tmem + ks * 8, bdesc, idesc_qk,
+                            (pass > 0 || ks > 0) ? 1u : 0u);
+              } else {
+                const uint64_t adesc =
+                    make_sdesc(qa + atom * BM * 128 + within, 16, 1024, kLayoutSw128);
+                mma_ss_f16(d_tmem, adesc, bdesc, idesc_qk, ks > 0 ? 1u : 0u);
               }
             }
-            tc_commit(bar_pv_done(t));
-            if (t == NQ - 1) tc_commit(bar_v_empty(sv));
           }
-          if (g + NSB < n_s) ok = issue_s(t, g + NSB);
+          if (t == NQ - 1) {
+            tc_commit(bar_k_empty(s));
+            if (g == w.n_s - 1) tc_commit(bar_q_empty);
+          }
+          tc_commit(bar_s_full(t, kg % NSB));
+          return true;
+        };
+
+        for (int g = 0; g < NSB && g < w.n_s && ok; ++g)
+          for (int t = 0; t < NQ && ok; ++t) ok = issue_s(t, g);
+        for (int g = 0; g < w.n_s && ok; ++g) {
+          for (int t = 0; t < NQ && ok; ++t) {
+            // the softmax warps of tile t are done with S_t(g) (and wrote P_t(g))
+            ok = wait(bar_p_full(t), (kc + g) & 1);
+            if (!ok) break;
+            if (in_pass2(g)) {
+              const int j = tile_of(g);
+              const int vg = vc + j;
+              const int sv = vg % VST;
+              if (t == 0) {
+                ok = wait(kSplit ? bar_v_ready(sv) : bar_v_full(sv), (vg / VST) & 1);
+                if (!ok) break;
+              }
+              // the first P@V of an item overwrites O: the previous item's
+              // epilogue must have read it
+              if (j == 0 && k > 0) {
+                ok = wait(bar_o_empty(t), (k - 1) & 1);
+                if (!ok) break;
+              }
+              tc_fence_after();
+              const uint32_t o_tmem = tmem + L::t_o(t);
+              const uint32_t vbuf = sbase + L::kV + sv * L::kVStage;
+              constexpr int kSteps = BN / L::kUmmaK;
+              constexpr int kPasses = kSplit ? 3 : 1;
+#pragma unroll
+              for (int pass = 0; pass < kPasses; ++pass) {
+                const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, (kc + g) % NSB)
+                                        : pass == 0 ? tmem + L::t_plo(t)
+                                                    : tmem + L::t_phi(t);
+                const uint32_t v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
+#pragma unroll
+                for (int ks = 0; ks < kSteps; ++ks) {
+                  // V is MN-major: K advances over 128-byte rows; LBO steps
+                  // across head_dim atoms, SBO across the swizzle's row groups.
+                  const uint64_t bdesc = make_sdesc(vbuf + v_off + ks * L::kUmmaK * 128,
+                                                    BN * 128, L::kVSbo, L::kVLayout);
+                  const uint32_t a_tmem = p_tmem + ks * 8;  // 8 columns per K step
+                  const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
+                  if constexpr (kSplit)
+                    mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+                  else
+                    mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+                }
+              }
+              tc_commit(bar_pv_done(t));
+              if (t == NQ - 1) tc_commit(bar_v_empty(sv));
+            }
+            if (g + NSB < w.n_s) ok = issue_s(t, g + NSB);
+          }
         }
+        kc += w.n_s;
+        vc += w.n_kv;
       }
       // make sure no MMA is still writing TMEM when the CTA tears down
       tc_commit(bar_drain);
@@ -550,57 +600,66 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       }
       fence_proxy_async_smem();
     };
-    bool ok = mbar_wait(bar_q_full, 0, abort_flag, p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
-                        kWaitLimitNs);
-    if (ok) {
-      // Q row r (TMEM lane r) -> hi / lo columns of the score MMA's A operand.
-      // Warp w may only touch TMEM lanes 32*(w%4)..+31, so each split warp
-      // moves the rows of its own lane quadrant.
-      const int quad = warp & 3;
-      const int r = quad * 32 + lane;
-      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-#pragma unroll 1
-      for (int a = 0; a < L::kAtoms; ++a) {
-        uint32_t qh[32], ql[32];
-        const uint8_t* row = smem + L::kQ + a * BM * 128 + r * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
-          const float4 x = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) * 16));
-          const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const uint32_t hb = __float_as_uint(xs[e]) & 0xFFFFE000u;
-            qh[c * 4 + e] = hb;
-            ql[c * 4 + e] = __float_as_uint(xs[e] - __uint_as_float(hb));
-          }
-        }
-        tmem_st32(tmem + lane_off + L::t_qhi(0) + a * 32, qh);
-        tmem_st32(tmem + lane_off + L::t_qlo(0) + a * 32, ql);
-      }
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar_q_ready);
-    }
-    // Split in the order the MMA consumes: K_0 .. K_{NSB-1}, then V_j, K_{j+NSB}.
-    auto split_k = [&](int j) -> bool {
-      const int s = j % KST;
-      if (!mbar_wait(bar_k_full(s), (j / KST) & 1, abort_flag, p.status,
-                     B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs))
-        return false;
-      split_tile(L::kK + s * L::kKStage, L::kKVBytes);
-      mbar_arrive(bar_k_ready(s));
-      return true;
-    };
-    for (int j = 0; j < NSB && j < n_kv && ok; ++j) ok = split_k(j);
-    for (int j = 0; j < n_kv && ok; ++j) {
-      const int sv = j % VST;
-      ok = mbar_wait(bar_v_full(sv), (j / VST) & 1, abort_flag, p.status,
-                     B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
+    bool ok = true;
+    int kc = 0, vc = 0;
+    for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+      const Item w = item_at(it);
+      ok = wait(bar_q_full, k & 1);
+      // the previous item's score MMAs read the Q operand in TMEM
+      if (ok && k > 0) ok = wait(bar_q_empty, (k - 1) & 1);
       if (!ok) break;
-      split_tile(L::kV + sv * L::kVStage, L::kKVBytes);
-      mbar_arrive(bar_v_ready(sv));
-      if (j + NSB < n_kv) ok = split_k(j + NSB);
+      {
+        // Q row r (TMEM lane r) -> hi / lo columns of the score MMA's A
+        // operand. Warp w may only touch TMEM lanes 32*(w%4)..+31, so each
+        // split warp moves the rows of its own lane quadrant.
+        tc_fence_after();
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+#pragma unroll 1
+        for (int a = 0; a < L::kAtoms; ++a) {
+          uint32_t qh[32], ql[32];
+          const uint8_t* row = smem + L::kQ + a * BM * 128 + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
+            const float4 x = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) * 16));
+            const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t hb = __float_as_uint(xs[e]) & 0xFFFFE000u;
+              qh[c * 4 + e] = hb;
+              ql[c * 4 + e] = __float_as_uint(xs[e] - __uint_as_float(hb));
+            }
+          }
+          tmem_st32(tmem + lane_off + L::t_qhi(0) + a * 32, qh);
+          tmem_st32(tmem + lane_off + L::t_qlo(0) + a * 32, ql);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_q_ready);
+      }
+      // Split in the order the MMA consumes: K_0 .. K_{NSB-1}, then V_j, K_{j+NSB}.
+      auto split_k = [&](int j) -> bool {
+        const int kg = kc + j;
+        const int s = kg % KST;
+        if (!wait(bar_k_full(s), (kg / KST) & 1)) return false;
+        split_tile(L::kK + s * L::kKStage, L::kKVBytes);
+        mbar_arrive(bar_k_ready(s));
+        return true;
+      };
+      for (int j = 0; j < NSB && j < w.n_kv && ok; ++j) ok = split_k(j);
+      for (int j = 0; j < w.n_kv && ok; ++j) {
+        const int vg = vc + j;
+        const int sv = vg % VST;
+        ok = wait(bar_v_full(sv), (vg / VST) & 1);
+        if (!ok) break;
+        split_tile(L::kV + sv * L::kVStage, L::kKVBytes);
+        mbar_arrive(bar_v_ready(sv));
+        if (j + NSB < w.n_kv) ok = split_k(j + NSB);
+      }
+      kc += w.n_s;
+      vc += w.n_kv;
     }
   } else if (warp < L::kSoftmaxWarps) {
     if constexpr (kTwoPass) {
@@ -614,210 +673,214 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       const int half = (warp >> 2) & 1;
       const int quad = warp & 3;
       const int r = quad * 32 + lane;
-      const int row0 = q0 + t * BM;
-      const int m = row0 + r;
       const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-      const int warp_row0 = row0 + quad * 32;
       const int c0 = half * HB;  // first key column of this thread within a tile
-      float m_run = -INFINITY;   // running max of this half, log2 units
-      float l_run = 0.f;
-      float m_fin = 0.f, inv_l = 0.f;  // row max (log2 units) and 1/row sum
-      bool ok = true;
       const float scale = p.scale;
       const bool pow2 = p.scale_pow2 != 0;
+      bool ok = true;
+      int kc = 0, vc = 0;
+      for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+        const Item w = item_at(it);
+        const int row0 = w.q0 + t * BM;
+        const int m = row0 + r;
+        const int warp_row0 = row0 + quad * 32;
+        float m_run = -INFINITY;  // running max of this half, log2 units
+        float l_run = 0.f;
+        float m_fin = 0.f, inv_l = 0.f;  // row max (log2 units) and 1/row sum
 
-      for (int g = 0; g < n_s && ok; ++g) {
-        const int buf = g % NSB;
-        const int j = tile_of(g);
-        const bool pass2 = in_pass2(g);
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full(t, buf), (g / NSB) & 1, abort_flag,
-                                               p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
-                                               kWaitLimitNs));
-        if (!ok) break;
-        tc_fence_after();
-        const int n0 = j * BN + c0;  // first key of this thread's columns
-        uint32_t raw[HB];
+        for (int g = 0; g < w.n_s && ok; ++g) {
+          const int sg = kc + g;
+          const int buf = sg % NSB;
+          const bool pass2 = g >= w.n_kv;
+          const int j = pass2 ? g - w.n_kv : g;
+          ok = __all_sync(0xFFFFFFFFu, wait(bar_s_full(t, buf), (sg / NSB) & 1));
+          if (!ok) break;
+          tc_fence_after();
+          const int n0 = j * BN + c0;  // first key of this thread's columns
+          uint32_t raw[HB];
 #pragma unroll
-        for (int c = 0; c < HB / 32; ++c)
-          tmem_ld32(tmem + lane_off + L::t_s(t, buf) + c0 + c * 32,
-                    *reinterpret_cast<uint32_t(*)[32]>(&raw[c * 32]));
-        uint32_t kbits[HB / 32];
-        if constexpr (HAS_MASK) {
+          for (int c = 0; c < HB / 32; ++c)
+            tmem_ld32(tmem + lane_off + L::t_s(t, buf) + c0 + c * 32,
+                      *reinterpret_cast<uint32_t(*)[32]>(&raw[c * 32]));
+          uint32_t kbits[HB / 32];
+          if constexpr (HAS_MASK) {
 #pragma unroll
-          for (int w = 0; w < HB / 32; ++w) {
-            const int n = n0 + w * 32 + lane;
-            bool valid = false;
-            if (n < p.seq) valid = p.mask[b * p.mask_sb + n * p.mask_ss] != 0;
-            kbits[w] = __ballot_sync(0xFFFFFFFFu, valid);
-          }
-        }
-        tc_wait_ld();
-        if (!pass2) {
-          // pass 1 keeps nothing in TMEM: the score buffer is free as soon as
-          // it has been read, so the next score tile overlaps this math.
-          tc_fence_before();
-          mbar_arrive(bar_p_full(t));
-        }
-        const bool masked = HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
-
-        // Scores with the reference's dtype boundaries, s = T(T(qk) * scale),
-        // as fp32 pairs; masked keys become -inf. `mx` = max over the half.
-        float sv[HB];
-        float mx;
-        if (!masked) {
-          uint32_t mx2 = 0xFF80FF80u;  // (-inf, -inf) in bf16; replaced below for fp16
-          if constexpr (std::is_same_v<T, __half>) mx2 = 0xFC00FC00u;
-#pragma unroll
-          for (int i = 0; i < HB; i += 2) {
-            uint32_t r1 = cvt_pack2<T>(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1]));
-            float a, c;
-            if (std::is_same_v<T, __nv_bfloat16> && pow2) {
-              // T(r1 * 2^k) == r1 * 2^k for bf16: the second rounding is exact
-              mx2 = max_pack2<T>(mx2, r1);
-              unpack2<T>(r1, a, c);
-              mul2(a, c, scale, scale);
-            } else {
-              unpack2<T>(r1, a, c);
-              mul2(a, c, scale, scale);
-              const uint32_t r2 = cvt_pack2<T>(a, c);
-              mx2 = max_pack2<T>(mx2, r2);
-              unpack2<T>(r2, a, c);
+            for (int wd = 0; wd < HB / 32; ++wd) {
+              const int n = n0 + wd * 32 + lane;
+              bool valid = false;
+              if (n < p.seq) valid = p.mask[w.b * p.mask_sb + n * p.mask_ss] != 0;
+              kbits[wd] = __ballot_sync(0xFFFFFFFFu, valid);
             }
-            sv[i] = a;
-            sv[i + 1] = c;
           }
-          float ma, mb;
-          unpack2<T>(mx2, ma, mb);
-          mx = fmaxf(ma, mb);
-          if (std::is_same_v<T, __nv_bfloat16> && pow2) mx *= scale;
-        } else {
-#pragma unroll
-          for (int i = 0; i < HB; i += 2) {
-            float a = __uint_as_float(raw[i]), c = __uint_as_float(raw[i + 1]);
-            round_pair<T>(a, c);
-            a *= scale;
-            c *= scale;
-            round_pair<T>(a, c);
-            sv[i] = a;
-            sv[i + 1] = c;
+          tc_wait_ld();
+          if (!pass2) {
+            // pass 1 keeps nothing in TMEM: the score buffer is free as soon
+            // as it has been read, so the next score tile overlaps this math.
+            tc_fence_before();
+            mbar_arrive(bar_p_full(t));
           }
-#pragma unroll
-          for (int i = 0; i < HB; ++i) {
-            const int n = n0 + i;
-            bool allowed;
-            if constexpr (HAS_MASK)
-              allowed = (kbits[i / 32] >> (i % 32)) & 1u;
-            else
-              allowed = n < p.seq;
-            if (CAUSAL) allowed = allowed && (n <= m);
-            sv[i] = allowed ? sv[i] : -INFINITY;
-          }
-          mx = row_max(sv);
-        }
+          const bool masked =
+              HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
 
-        if (!pass2) {
-          // pass 1: running max and sum of this half
-          const float m_new = fmaxf(m_run, mx * kLog2e);
-          const float m_use = m_new == -INFINITY ? 0.f : m_new;
-          const float alpha = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_use);
-          float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          // Scores with the reference's dtype boundaries, s = T(T(qk) * scale),
+          // as fp32 pairs; masked keys become -inf. `mx` = max over the half.
+          float sv[HB];
+          float mx;
+          if (!masked) {
+            uint32_t mx2 = std::is_same_v<T, __half> ? 0xFC00FC00u : 0xFF80FF80u;  // (-inf, -inf)
+#pragma unroll
+            for (int i = 0; i < HB; i += 2) {
+              uint32_t r1 = cvt_pack2<T>(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1]));
+              float a, c;
+              if (std::is_same_v<T, __nv_bfloat16> && pow2) {
+                // T(r1 * 2^k) == r1 * 2^k for bf16: the second rounding is exact
+                mx2 = max_pack2<T>(mx2, r1);
+                unpack2<T>(r1, a, c);
+                mul2(a, c, scale, scale);
+              } else {
+                unpack2<T>(r1, a, c);
+                mul2(a, c, scale, scale);
+                const uint32_t r2 = cvt_pack2<T>(a, c);
+                mx2 = max_pack2<T>(mx2, r2);
+                unpack2<T>(r2, a, c);
+              }
+              sv[i] = a;
+              sv[i + 1] = c;
+            }
+            float ma, mb;
+            unpack2<T>(mx2, ma, mb);
+            mx = fmaxf(ma, mb);
+            if (std::is_same_v<T, __nv_bfloat16> && pow2) mx *= scale;
+          } else {
+#pragma unroll
+            for (int i = 0; i < HB; i += 2) {
+              float a = __uint_as_float(raw[i]), c = __uint_as_float(raw[i + 1]);
+              round_pair<T>(a, c);
+              a *= scale;
+              c *= scale;
+              round_pair<T>(a, c);
+              sv[i] = a;
+              sv[i + 1] = c;
+            }
+#pragma unroll
+            for (int i = 0; i < HB; ++i) {
+              const int n = n0 + i;
+              bool allowed;
+              if constexpr (HAS_MASK)
+                allowed = (kbits[i / 32] >> (i % 32)) & 1u;
+              else
+                allowed = n < p.seq;
+              if (CAUSAL) allowed = allowed && (n <= m);
+              sv[i] = allowed ? sv[i] : -INFINITY;
+            }
+            mx = row_max(sv);
+          }
+
+          if (!pass2) {
+            // pass 1: running max and sum of this half
+            const float m_new = fmaxf(m_run, mx * kLog2e);
+            const float m_use = m_new == -INFINITY ? 0.f : m_new;
+            const float alpha = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_use);
+            float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int i = 0; i < HB; i += 2) {
+              float a = sv[i], c = sv[i + 1];
+              fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
+              a = ex2_approx(a);
+              c = ex2_approx(c);
+              add2(part[i % 8], part[i % 8 + 1], a, c);
+            }
+            add2(part[0], part[1], part[2], part[3]);
+            add2(part[4], part[5], part[6], part[7]);
+            add2(part[0], part[1], part[4], part[5]);
+            l_run = l_run * alpha + (part[0] + part[1]);
+            m_run = m_new;
+            if (j == w.n_kv - 1) {
+              // combine the two halves of the row (once per item)
+              float2* stats = reinterpret_cast<float2*>(smem + L::kStats);
+              stats[(t * 2 + half) * BM + r] = make_float2(m_run, l_run);
+              mbar_arrive(bar_stats(t));
+              ok = __all_sync(0xFFFFFFFFu, wait(bar_stats(t), k & 1));
+              if (!ok) break;
+              const float2 other = stats[(t * 2 + (half ^ 1)) * BM + r];
+              const float mm = fmaxf(m_run, other.x);
+              const float mu = mm == -INFINITY ? 0.f : mm;
+              const float la = m_run == -INFINITY ? 0.f : l_run * ex2_approx(m_run - mu);
+              const float lb = other.x == -INFINITY ? 0.f : other.y * ex2_approx(other.x - mu);
+              // same association on both threads of the row: (half 0) + (half 1)
+              const float l = half == 0 ? la + lb : lb + la;
+              m_fin = mu;
+              inv_l = l > 0.f ? 1.f / l : 0.f;
+            }
+            continue;
+          }
+
+          // pass 2: normalised probabilities, rounded to T, into TMEM
+          uint32_t pk[HB / 2];
 #pragma unroll
           for (int i = 0; i < HB; i += 2) {
             float a = sv[i], c = sv[i + 1];
-            fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
+            fma2(a, c, kLog2e, kLog2e, -m_fin, -m_fin);
             a = ex2_approx(a);
             c = ex2_approx(c);
-            add2(part[i % 8], part[i % 8 + 1], a, c);
+            mul2(a, c, inv_l, inv_l);
+            pk[i / 2] = cvt_pack2<T>(a, c);
           }
-          add2(part[0], part[1], part[2], part[3]);
-          add2(part[4], part[5], part[6], part[7]);
-          add2(part[0], part[1], part[4], part[5]);
-          l_run = l_run * alpha + (part[0] + part[1]);
-          m_run = m_new;
-          if (j == n_kv - 1) {
-            // combine the two halves of the row (once per CTA)
-            float2* stats = reinterpret_cast<float2*>(smem + L::kStats);
-            stats[(t * 2 + half) * BM + r] = make_float2(m_run, l_run);
-            mbar_arrive(bar_stats(t));
-            ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_stats(t), 0, abort_flag, p.status,
-                                                   B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs));
-            if (!ok) break;
-            const float2 other = stats[(t * 2 + (half ^ 1)) * BM + r];
-            const float mm = fmaxf(m_run, other.x);
-            const float mu = mm == -INFINITY ? 0.f : mm;
-            const float la = m_run == -INFINITY ? 0.f : l_run * ex2_approx(m_run - mu);
-            const float lb = other.x == -INFINITY ? 0.f : other.y * ex2_approx(other.x - mu);
-            // same association on both threads of the row: (half 0) + (half 1)
-            const float l = half == 0 ? la + lb : lb + la;
-            m_fin = mu;
-            inv_l = l > 0.f ? 1.f / l : 0.f;
+          if (j > 0) {
+            // PV_{j-1} must have read P_{j-1} (same TMEM columns). Waiting
+            // for every P@V phase in order also keeps the pv_done parity
+            // barrier at most one phase ahead of this wait.
+            if (!__all_sync(0xFFFFFFFFu, wait(bar_pv_done(t), (vc + j - 1) & 1))) {
+              ok = false;
+              break;
+            }
           }
-          continue;
+#pragma unroll
+          for (int c = 0; c < HB / 64; ++c)
+            tmem_st32(tmem + lane_off + L::t_s(t, buf) + c0 / 2 + c * 32,
+                      *reinterpret_cast<const uint32_t(*)[32]>(&pk[c * 32]));
+          if constexpr (HB % 64 != 0)
+            tmem_st16(tmem + lane_off + L::t_s(t, buf) + c0 / 2 + (HB / 64) * 32,
+                      &pk[(HB / 64) * 32]);
+          tc_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar_p_full(t));
         }
 
-        // pass 2: normalised probabilities, rounded to T, into TMEM
-        uint32_t pk[HB / 2];
-#pragma unroll
-        for (int i = 0; i < HB; i += 2) {
-          float a = sv[i], c = sv[i + 1];
-          fma2(a, c, kLog2e, kLog2e, -m_fin, -m_fin);
-          a = ex2_approx(a);
-          c = ex2_approx(c);
-          mul2(a, c, inv_l, inv_l);
-          pk[i / 2] = cvt_pack2<T>(a, c);
-        }
-        if (j > 0) {
-          // PV_{j-1} must have read P_{j-1} (same TMEM columns) and keeps the
-          // pv_done parity barrier at most one phase ahead
-          const bool done = mbar_wait(bar_pv_done(t), (j - 1) & 1, abort_flag, p.status,
-                                      B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-          if (!__all_sync(0xFFFFFFFFu, done)) {
-            ok = false;
-            break;
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < HB / 64; ++c)
-          tmem_st32(tmem + lane_off + L::t_s(t, buf) + c0 / 2 + c * 32,
-                    *reinterpret_cast<const uint32_t(*)[32]>(&pk[c * 32]));
-        if constexpr (HB % 64 != 0)
-          tmem_st16(tmem + lane_off + L::t_s(t, buf) + c0 / 2 + (HB / 64) * 32,
-                    &pk[(HB / 64) * 32]);
-        tc_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar_p_full(t));
-      }
-
-      // epilogue: this thread stores head_dim columns [half*D/2, (half+1)*D/2)
-      if (ok) {
-        ok = mbar_wait(bar_pv_done(t), (n_kv - 1) & 1, abort_flag, p.status,
-                       B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-        ok = __all_sync(0xFFFFFFFFu, ok);
-      }
-      if (ok) {
-        tc_fence_after();
-        constexpr int DH = D / 2;
-        T* out_row = reinterpret_cast<T*>(p.out) +
-                     ((static_cast<int64_t>(b) * p.seq + m) * p.heads + h) * D + half * DH;
-        const bool row_ok = m < p.seq;
+        // epilogue: this thread stores head_dim columns [half*D/2, (half+1)*D/2)
+        if (ok) ok = __all_sync(0xFFFFFFFFu, wait(bar_pv_done(t), (vc + w.n_kv - 1) & 1));
+        if (ok) {
+          tc_fence_after();
+          constexpr int DH = D / 2;
+          T* out_row = reinterpret_cast<T*>(p.out) +
+                       ((static_cast<int64_t>(w.b) * p.seq + m) * p.heads + w.h) * D + half * DH;
+          const bool row_ok = m < p.seq;
 #pragma unroll 1
-        for (int c = 0; c < DH / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_off + L::t_o(t) + half * DH + c * 32, o);
-          tc_wait_ld();
-          if (row_ok) {
-            uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
+          for (int c = 0; c < DH / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_off + L::t_o(t) + half * DH + c * 32, o);
+            tc_wait_ld();
+            if (c == DH / 32 - 1) {
+              // O has been read: the next item's first P@V may overwrite it
+              tc_fence_before();
+              mbar_arrive(bar_o_empty(t));
+            }
+            if (row_ok) {
+              uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v;
-              v.x = cvt_pack2<T>(__uint_as_float(o[8 * i + 0]), __uint_as_float(o[8 * i + 1]));
-              v.y = cvt_pack2<T>(__uint_as_float(o[8 * i + 2]), __uint_as_float(o[8 * i + 3]));
-              v.z = cvt_pack2<T>(__uint_as_float(o[8 * i + 4]), __uint_as_float(o[8 * i + 5]));
-              v.w = cvt_pack2<T>(__uint_as_float(o[8 * i + 6]), __uint_as_float(o[8 * i + 7]));
-              dst[i] = v;
+              for (int i = 0; i < 4; ++i) {
+                uint4 v;
+                v.x = cvt_pack2<T>(__uint_as_float(o[8 * i + 0]), __uint_as_float(o[8 * i + 1]));
+                v.y = cvt_pack2<T>(__uint_as_float(o[8 * i + 2]), __uint_as_float(o[8 * i + 3]));
+                v.z = cvt_pack2<T>(__uint_as_float(o[8 * i + 4]), __uint_as_float(o[8 * i + 5]));
+                v.w = cvt_pack2<T>(__uint_as_float(o[8 * i + 6]), __uint_as_float(o[8 * i + 7]));
+                dst[i] = v;
+              }
             }
           }
         }
+        kc += w.n_s;
+        vc += w.n_kv;
       }
     } else {
       // ------------------------------------------ softmax, fp32 (one pass)
@@ -831,159 +894,168 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       const int half = (warp >> 2) & 1;
       const int quad = warp & 3;
       const int r = quad * 32 + lane;
-      const int row0 = q0;
-      const int m = row0 + r;
       const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-      const int warp_row0 = row0 + quad * 32;
       const int c0 = half * HB;
       float* xchg = reinterpret_cast<float*>(smem + L::kStats);  // [2 slots][2 halves][BM]
-      float m_ref = -INFINITY;  // running max of the row, log2 units
-      float l_sum = 0.f;        // partial sum of this half
-      bool ok = true;
       const float scale = p.scale;
+      bool ok = true;
+      int kc = 0, vc = 0, xc = 0;  // xc: completions of the exchange barrier so far
+      for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+        const Item w = item_at(it);
+        const int row0 = w.q0;
+        const int m = row0 + r;
+        const int warp_row0 = row0 + quad * 32;
+        float m_ref = -INFINITY;  // running max of the row, log2 units
+        float l_sum = 0.f;        // partial sum of this half
 
-      for (int j = 0; j < n_s && ok; ++j) {
-        const int buf = j % NSB;
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_s_full(0, buf), (j / NSB) & 1, abort_flag,
-                                               p.status, B200TK_STATUS_PIPELINE_TIMEOUT,
-                                               kWaitLimitNs));
-        if (!ok) break;
-        tc_fence_after();
-        const int n0 = j * BN + c0;
-        float sv[HB];
-        {
-          uint32_t raw[HB];
-          tmem_ld_cols<HB>(tmem + lane_off + L::t_s(0, buf) + c0, raw);
-          uint32_t kbits = 0xFFFFFFFFu;
-          if constexpr (HAS_MASK) {
-            const int n = n0 + lane;
-            bool valid = false;
-            if (n < p.seq) valid = p.mask[b * p.mask_sb + n * p.mask_ss] != 0;
-            kbits = __ballot_sync(0xFFFFFFFFu, valid);
-          }
-          tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < HB; ++i) sv[i] = __uint_as_float(raw[i]) * scale;
-          const bool masked =
-              HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
-          if (masked) {
-#pragma unroll
-            for (int i = 0; i < HB; ++i) {
-              const int n = n0 + i;
-              bool allowed = HAS_MASK ? ((kbits >> i) & 1u) != 0 : n < p.seq;
-              if (CAUSAL) allowed = allowed && (n <= m);
-              sv[i] = allowed ? sv[i] : -INFINITY;
-            }
-          }
-        }
-        // row max over both halves
-        float mx = row_max(sv);
-        xchg[((j & 1) * 2 + half) * BM + r] = mx;
-        mbar_arrive(bar_stats(0));
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_stats(0), j & 1, abort_flag, p.status,
-                                               B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs));
-        if (!ok) break;
-        mx = fmaxf(mx, xchg[((j & 1) * 2 + (half ^ 1)) * BM + r]);
-
-        const float m_new = fmaxf(m_ref, mx * kLog2e);  // -inf stays -inf
-        bool rescale = false;
-        float alpha = 1.f;
-        if (j == 0) {
-          m_ref = m_new;
-        } else if (__any_sync(0xFFFFFFFFu, m_new > m_ref + kRescaleThreshold)) {
-          // the running max grew by more than 2^8: move every row of this
-          // warp to its new max (rows whose max did not grow keep alpha = 1).
-          // The partner warp sees the same maxima and decides the same way.
-          rescale = true;
-          if (m_new > m_ref) {
-            alpha = ex2_approx(m_ref - m_new);
-            m_ref = m_new;
-          }
-          l_sum *= alpha;
-        }
-        const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-        float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int i = 0; i < HB; i += 2) {
-          float a = sv[i], c = sv[i + 1];
-          fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
-          a = ex2_approx(a);
-          c = ex2_approx(c);
-          sv[i] = a;
-          sv[i + 1] = c;
-          add2(part[i % 8], part[i % 8 + 1], a, c);
-        }
-        add2(part[0], part[1], part[2], part[3]);
-        add2(part[4], part[5], part[6], part[7]);
-        add2(part[0], part[1], part[4], part[5]);
-        l_sum += part[0] + part[1];
-        // pv_done is a parity barrier: it only tells the current phase from
-        // the previous one. Waiting for every P@V phase in order (PV_{j-1}
-        // before storing P_j) keeps it at most one phase ahead, keeps P_{j-1}
-        // alive until its MMA has read it, and orders the O rescale after the
-        // MMA that wrote O.
-        if (j > 0) {
-          const bool done = mbar_wait(bar_pv_done(0), (j - 1) & 1, abort_flag, p.status,
-                                      B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-          if (!__all_sync(0xFFFFFFFFu, done)) {
-            ok = false;
-            break;
-          }
-        }
-        if (rescale) {
+        for (int j = 0; j < w.n_s && ok; ++j) {
+          const int sg = kc + j;
+          const int buf = sg % NSB;
+          ok = __all_sync(0xFFFFFFFFu, wait(bar_s_full(0, buf), (sg / NSB) & 1));
+          if (!ok) break;
           tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < DH / 32; ++c) {
-            uint32_t o[32];
-            const uint32_t addr = tmem + lane_off + L::t_o(0) + half * DH + c * 32;
-            tmem_ld32(addr, o);
+          const int n0 = j * BN + c0;
+          float sv[HB];
+          {
+            uint32_t raw[HB];
+            tmem_ld_cols<HB>(tmem + lane_off + L::t_s(0, buf) + c0, raw);
+            uint32_t kbits = 0xFFFFFFFFu;
+            if constexpr (HAS_MASK) {
+              const int n = n0 + lane;
+              bool valid = false;
+              if (n < p.seq) valid = p.mask[w.b * p.mask_sb + n * p.mask_ss] != 0;
+              kbits = __ballot_sync(0xFFFFFFFFu, valid);
+            }
             tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(addr, o);
-          }
-        }
-        {
-          // P hi keeps the tf32 bits, P lo the exact remainder
-          uint32_t ph[HB], pl[HB];
+            for (int i = 0; i < HB; ++i) sv[i] = __uint_as_float(raw[i]) * scale;
+            const bool masked =
+                HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
+            if (masked) {
 #pragma unroll
-          for (int i = 0; i < HB; ++i) {
-            const uint32_t hb = __float_as_uint(sv[i]) & 0xFFFFE000u;
-            ph[i] = hb;
-            pl[i] = __float_as_uint(sv[i] - __uint_as_float(hb));
+              for (int i = 0; i < HB; ++i) {
+                const int n = n0 + i;
+                bool allowed = HAS_MASK ? ((kbits >> i) & 1u) != 0 : n < p.seq;
+                if (CAUSAL) allowed = allowed && (n <= m);
+                sv[i] = allowed ? sv[i] : -INFINITY;
+              }
+            }
           }
-          tmem_st_cols<HB>(tmem + lane_off + L::t_phi(0) + c0, ph);
-          tmem_st_cols<HB>(tmem + lane_off + L::t_plo(0) + c0, pl);
-        }
-        tc_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar_p_full(0));
-      }
+          // row max over both halves
+          float mx = row_max(sv);
+          const int slot = xc & 1;
+          xchg[(slot * 2 + half) * BM + r] = mx;
+          mbar_arrive(bar_stats(0));
+          ok = __all_sync(0xFFFFFFFFu, wait(bar_stats(0), xc & 1));
+          ++xc;
+          if (!ok) break;
+          mx = fmaxf(mx, xchg[(slot * 2 + (half ^ 1)) * BM + r]);
 
-      // epilogue: combine the two partial row sums, store this half of O
-      if (ok) {
-        xchg[((n_s & 1) * 2 + half) * BM + r] = l_sum;
-        mbar_arrive(bar_stats(0));
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar_stats(0), n_s & 1, abort_flag, p.status,
-                                               B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs));
-      }
-      if (ok) {
-        const float other = xchg[((n_s & 1) * 2 + (half ^ 1)) * BM + r];
-        const float l = half == 0 ? l_sum + other : other + l_sum;
-        ok = mbar_wait(bar_pv_done(0), (n_kv - 1) & 1, abort_flag, p.status,
-                       B200TK_STATUS_PIPELINE_TIMEOUT, kWaitLimitNs);
-        ok = __all_sync(0xFFFFFFFFu, ok);
+          const float m_new = fmaxf(m_ref, mx * kLog2e);  // -inf stays -inf
+          bool rescale = false;
+          float alpha = 1.f;
+          if (j == 0) {
+            m_ref = m_new;
+          } else if (__any_sync(0xFFFFFFFFu, m_new > m_ref + kRescaleThreshold)) {
+            // the running max grew by more than 2^8: move every row of this
+            // warp to its new max (rows whose max did not grow keep alpha = 1).
+            // The partner warp sees the same maxima and decides the same way.
+            rescale = true;
+            if (m_new > m_ref) {
+              alpha = ex2_approx(m_ref - m_new);
+              m_ref = m_new;
+            }
+            l_sum *= alpha;
+          }
+          const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+          float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int i = 0; i < HB; i += 2) {
+            float a = sv[i], c = sv[i + 1];
+            fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
+            a = ex2_approx(a);
+            c = ex2_approx(c);
+            sv[i] = a;
+            sv[i + 1] = c;
+            add2(part[i % 8], part[i % 8 + 1], a, c);
+          }
+          add2(part[0], part[1], part[2], part[3]);
+          add2(part[4], part[5], part[6], part[7]);
+          add2(part[0], part[1], part[4], part[5]);
+          l_sum += part[0] + part[1];
+          // pv_done is a parity barrier: it only tells the current phase from
+          // the previous one. Waiting for every P@V phase in order (PV_{j-1}
+          // before storing P_j) keeps it at most one phase ahead, keeps P_{j-1}
+          // alive until its MMA has read it, and orders the O rescale after
+          // the MMA that wrote O.
+          if (j > 0) {
+            if (!__all_sync(0xFFFFFFFFu, wait(bar_pv_done(0), (vc + j - 1) & 1))) {
+              ok = false;
+              break;
+            }
+          }
+          if (rescale) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < DH / 32; ++c) {
+              uint32_t o[32];
+              const uint32_t addr = tmem + lane_off + L::t_o(0) + half * DH + c * 32;
+              tmem_ld32(addr, o);
+              tc_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st32(addr, o);
+            }
+          }
+          {
+            // P hi keeps the tf32 bits, P lo the exact remainder
+            uint32_t ph[HB], pl[HB];
+#pragma unroll
+            for (int i = 0; i < HB; ++i) {
+              const uint32_t hb = __float_as_uint(sv[i]) & 0xFFFFE000u;
+              ph[i] = hb;
+              pl[i] = __float_as_uint(sv[i] - __uint_as_float(hb));
+            }
+            tmem_st_cols<HB>(tmem + lane_off + L::t_phi(0) + c0, ph);
+            tmem_st_cols<HB>(tmem + lane_off + L::t_plo(0) + c0, pl);
+          }
+          tc_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar_p_full(0));
+        }
+
+        // epilogue: combine the two partial row sums, store this half of O
+        float l = 0.f;
+        if (ok) {
+          const int slot = xc & 1;
+          xchg[(slot * 2 + half) * BM + r] = l_sum;
+          mbar_arrive(bar_stats(0));
+          ok = __all_sync(0xFFFFFFFFu, wait(bar_stats(0), xc & 1));
+          ++xc;
+          if (ok) {
+            const float other = xchg[(slot * 2 + (half ^ 1)) * BM + r];
+            l = half == 0 ? l_sum + other : other + l_sum;
+          }
+        }
+        if (ok) ok = __all_sync(0xFFFFFFFFu, wait(bar_pv_done(0), (vc + w.n_kv - 1) & 1));
         if (ok) {
           tc_fence_after();
           const float out_scale = l > 0.f ? 1.f / l : 0.f;
           float* out_row = reinterpret_cast<float*>(p.out) +
-                           ((static_cast<int64_t>(b) * p.seq + m) * p.heads + h) * D + half * DH;
+                           ((static_cast<int64_t>(w.b) * p.seq + m) * p.heads + w.h) * D +
+                           half * DH;
           const bool row_ok = m < p.seq;
 #pragma unroll 1
           for (int c = 0; c < DH / 32; ++c) {
             uint32_t o[32];
             tmem_ld32(tmem + lane_off + L::t_o(0) + half * DH + c * 32, o);
             tc_wait_ld();
+            if (c == DH / 32 - 1) {
+              // O has been read: the next item's first P@V may overwrite it
+              tc_fence_before();
+              mbar_arrive(bar_o_empty(0));
+            }
             if (row_ok) {
               float4* dst = reinterpret_cast<float4*>(out_row + c * 32);
 #pragma unroll
@@ -998,6 +1070,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             }
           }
         }
+        kc += w.n_s;
+        vc += w.n_kv;
       }
     }
   }
@@ -1043,13 +1117,20 @@ struct TcTile<float, 128> {
 // Fills the grid-dependent parameters and launches the instantiation for
 // (causal, mask).
 template <typename T, int D>
-cudaError_t launch_dtype_hd(AttnTcParams prm, bool causal, bool has_mask, cudaStream_t stream) {
+cudaError_t launch_dtype_hd(AttnTcParams prm, int num_sms, bool causal, bool has_mask,
+                            cudaStream_t stream) {
   using C = TcTile<T, D>;
   const int rows_per_cta = C::kNQ * BM;
   prm.n_qtiles = (prm.seq + rows_per_cta - 1) / rows_per_cta;
-  const int64_t grid64 = static_cast<int64_t>(prm.n_qtiles) * prm.batch * prm.heads;
-  if (grid64 > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
-  const int grid = static_cast<int>(grid64);
+  const int64_t items = static_cast<int64_t>(prm.n_qtiles) * prm.batch * prm.heads;
+  if (items > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
+  // Non-causal items all cost the same: one persistent CTA per SM loops over
+  // them (barriers and TMEM set up once, the next item's loads overlap the
+  // current item's tail). Causal items differ in length by up to the number
+  // of query tiles; a CTA per item lets the hardware block scheduler balance
+  // them (longest first), which a static round-robin assignment cannot.
+  const int grid =
+      static_cast<int>(causal ? items : (items < num_sms ? items : static_cast<int64_t>(num_sms)));
   if (causal)
     return has_mask
                ? launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, true, true>(prm, grid, stream)
@@ -1062,7 +1143,7 @@ cudaError_t launch_dtype_hd(AttnTcParams prm, bool causal, bool has_mask, cudaSt
 // Explicit instantiations live in attention_tc_inst.cu, compiled once per
 // (dtype, head_dim) so the six variants build in parallel.
 #define B200TK_TC_DECLARE(T, D) \
-  extern template cudaError_t launch_dtype_hd<T, D>(AttnTcParams, bool, bool, cudaStream_t);
+  extern template cudaError_t launch_dtype_hd<T, D>(AttnTcParams, int, bool, bool, cudaStream_t);
 B200TK_TC_DECLARE(__nv_bfloat16, 64)
 B200TK_TC_DECLARE(__nv_bfloat16, 128)
 B200TK_TC_DECLARE(__half, 64)

@@ -18,7 +18,7 @@
 
 namespace b200tk {
 namespace tc {
-template cudaError_t launch_dtype_hd<B200TK_TC_T, B200TK_TC_HEAD_DIM>(AttnTcParams, bool, bool,
-                                                                      cudaStream_t);
+template cudaError_t launch_dtype_hd<B200TK_TC_T, B200TK_TC_HEAD_DIM>(AttnTcParams, int, bool,
+                                                                      bool, cudaStream_t);
 }  // namespace tc
 }  // namespace b200tk
