@@ -355,7 +355,8 @@ def run_b200_arm(args) -> int:
     timer.wrap(_native)
 
     torch.manual_seed(0)
-    model = UserOptimizedTransformer(TransformerConfig(b, s, d, h, f, layers, causal))
+    model = UserOptimizedTransformer(TransformerConfig(b, s, d, h, f, layers, causal),
+                                     execution_mode=args.execution_mode)
     model = model.to(device=device, dtype=dtype).eval()
     cfg = oracle.TransformerConfig(b, s, d, h, f, layers, causal)
     x, _ = oracle.generate_random_case(cfg, device, dtype, 1 + rank)  # this rank's batch
@@ -369,11 +370,10 @@ def run_b200_arm(args) -> int:
         torch.cuda.synchronize(device)
         _native.device_status(local, clear=True)
 
-        # ---- device-resident timed region
+        # ---- device-resident timed region (the model in its execution mode)
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        launches_before = timer.launches
-        timer.enabled = True
+        replays_before = model.cuda_graph_replays
         barrier(world)
         torch.cuda.synchronize(device)
         with ClockSampler(local) as clocks:
@@ -384,13 +384,30 @@ def run_b200_arm(args) -> int:
                 ends[i].record(stream)
             torch.cuda.synchronize(device)
             barrier(world)
-        timer.enabled = False
-        launches = timer.launches - launches_before
+        graphed = model.cuda_graph_replays - replays_before == args.steps
         step_ms = [st.elapsed_time(en) for st, en in zip(starts, ends)]
         local_ms = sum(step_ms) / len(step_ms)
         from transformer_opt.sharding import gather_stats, max_over_ranks
 
         ms_per_step = max_over_ranks(local_ms, device)
+
+        # ---- per-kernel events: graph replays launch without passing through
+        # the ctypes entry points, so the kernels are timed in an eager pass
+        # that issues the same launches in the same order.
+        mode = model.execution_mode
+        model.execution_mode = "eager"
+        launches_before = timer.launches
+        timer.enabled = True
+        barrier(world)
+        torch.cuda.synchronize(device)
+        for _ in range(args.steps):
+            flush.zero_()
+            model(x)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        timer.enabled = False
+        model.execution_mode = mode
+        launches = timer.launches - launches_before
         attn_ms = timer.mean_ms("attention")
         rln_ms = timer.mean_ms("rln")
         rln_bytes = timer.rln_bytes_per_launch()
@@ -467,6 +484,8 @@ def run_b200_arm(args) -> int:
             "seq_len": s,
             "parallelism": f"dp{world} (batch shards, weights replicated, no collective)",
             "l2": "flushed between timed steps (256 MiB write)",
+            "execution_mode": args.execution_mode,
+            "cuda_graph": graphed,
         },
         "e2e": {
             "value": tokens / (e2e_ms / 1000.0),
@@ -514,6 +533,8 @@ def main() -> int:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--config", choices=sorted(CONFIGS), default="C2")
+    parser.add_argument("--execution-mode", choices=("auto", "eager", "graph"), default="auto",
+                        help="UserOptimizedTransformer execution_mode")
     parser.add_argument("--no-validate", dest="validate", action="store_false")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--ref-budget", type=float, default=15.0,

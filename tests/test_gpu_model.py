@@ -191,3 +191,70 @@ def test_small_head_dims_run_the_generic_kernel_inside_the_model():
         res = oracle.compare_outputs(baseline(x), optimized(x))
     assert res.passed, res
     assert optimized.attention_backend_counts["b200"] == 2
+
+
+def _graph_pair(mode, dtype=torch.float32, shape=(2, 128, 256, 4, 1024, 2, True)):
+    torch.manual_seed(3)
+    model = UserOptimizedTransformer(TransformerConfig(*shape), execution_mode=mode)
+    return model.to(device="cuda", dtype=dtype).eval()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_graph_replay_matches_eager_and_takes_fresh_inputs(dtype):
+    graph = _graph_pair("graph", dtype)
+    eager = _graph_pair("eager", dtype)
+    eager.load_state_dict(graph.state_dict())
+    g = torch.Generator(device="cuda").manual_seed(0)
+    xs = [torch.randn(2, 128, 256, device="cuda", generator=g).to(dtype) for _ in range(3)]
+    with torch.inference_mode():
+        outs = [graph(x) for x in xs]
+        refs = [eager(x) for x in xs]
+    for out, ref in zip(outs, refs):
+        assert torch.equal(out, ref)  # same kernels, same order: bitwise
+    assert not torch.equal(outs[0], outs[1])  # results are not aliased
+    assert graph.cuda_graph_replays == 3
+    assert graph.attention_backend_counts["b200"] == 3 * 2
+    assert graph.fused_residual_layer_norm_calls == 3 * 4
+
+
+def test_graph_recaptures_after_parameter_update_and_mask_change():
+    graph = _graph_pair("graph")
+    eager = _graph_pair("eager")
+    eager.load_state_dict(graph.state_dict())
+    x = torch.randn(2, 128, 256, device="cuda")
+    mask = torch.arange(128, device="cuda")[None, :] < torch.tensor([[128], [77]], device="cuda")
+    with torch.inference_mode():
+        first = graph(x)
+    with torch.no_grad():
+        for model in (graph, eager):
+            model.layers[0].ffn_in.weight.mul_(1.5)
+    with torch.inference_mode():
+        updated = graph(x)
+        assert torch.equal(updated, eager(x))
+        assert not torch.equal(first, updated)
+        masked = graph(x, mask)
+        assert torch.equal(masked, eager(x, mask))
+        assert torch.count_nonzero(masked[1, 77:]) == 0
+
+
+def test_auto_mode_replays_only_launch_bound_forwards():
+    small = _graph_pair("auto", shape=(2, 128, 256, 4, 1024, 1, False))
+    big = _graph_pair("auto", shape=(8, 1024, 1024, 16, 1024, 1, False))
+    with torch.inference_mode():
+        small(torch.randn(2, 128, 256, device="cuda"))
+        big(torch.randn(8, 1024, 1024, device="cuda"))
+    assert small.cuda_graph_replays == 1
+    assert big.cuda_graph_replays == 0
+
+
+def test_graph_switches_between_no_grad_and_inference_mode():
+    graph = _graph_pair("graph")
+    x = torch.randn(2, 128, 256, device="cuda")
+    with torch.inference_mode():
+        a = graph(x)
+    with torch.no_grad():
+        b = graph(x)
+    with torch.inference_mode():
+        c = graph(x)
+    assert torch.equal(a, b) and torch.equal(b, c)
+    assert graph.cuda_graph_replays == 3

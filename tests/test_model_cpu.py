@@ -87,6 +87,17 @@ def test_constructor_validation():
         UserOptimizedTransformer(cfg, attention_backend="mystery")
     with pytest.raises(ValueError, match="execution_mode"):
         UserOptimizedTransformer(cfg, execution_mode="never")
+    for mode in ("auto", "eager", "graph"):
+        assert UserOptimizedTransformer(cfg, execution_mode=mode).execution_mode == mode
+
+
+def test_graph_mode_on_cpu_runs_the_explicit_forward():
+    cfg = TransformerConfig(1, 8, 16, 2, 32, 1, False)
+    model = UserOptimizedTransformer(cfg, execution_mode="graph").eval()
+    with torch.inference_mode():
+        out = model(torch.randn(1, 8, 16))
+    assert out.shape == (1, 8, 16)
+    assert model.cuda_graph_replays == 0
 
 
 def test_fused_route_reason_on_cpu():

@@ -1,6 +1,7 @@
 // attention_tc.cu - host-side launcher of the tcgen05 attention kernels
 // (kernel: attention_tc.cuh): fills the kernel parameter block and picks the
 // (dtype, head_dim, causal, mask) instantiation.
+#include <atomic>
 #include <cmath>
 
 #include "attention_tc.cuh"
@@ -38,11 +39,18 @@ cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
   const bool has_mask = a.mask != nullptr;
   const bool d64 = a.head_dim == 64;
   if (a.head_dim != 64 && a.head_dim != 128) return cudaErrorInvalidValue;
-  int device = 0, num_sms = 0;
+  // SM count per device, queried once (no device queries on later launches)
+  static std::atomic<int> sm_count[64] = {};
+  int device = 0;
   cudaError_t err = cudaGetDevice(&device);
-  if (err == cudaSuccess)
-    err = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device);
   if (err != cudaSuccess) return err;
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  int num_sms = sm_count[device].load(std::memory_order_relaxed);
+  if (num_sms == 0) {
+    err = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (err != cudaSuccess) return err;
+    sm_count[device].store(num_sms, std::memory_order_relaxed);
+  }
   switch (a.dtype) {
     case B200TK_DTYPE_BFLOAT16:
       return d64 ? tc::launch_dtype_hd<__nv_bfloat16, 64>(prm, num_sms, causal, has_mask, stream)

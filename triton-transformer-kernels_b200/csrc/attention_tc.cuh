@@ -34,6 +34,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <type_traits>
 
@@ -1091,8 +1092,19 @@ cudaError_t launch_tc(const AttnTcParams& prm, int grid, cudaStream_t stream) {
   auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, CAUSAL, HAS_MASK>;
   // at least ~116 KB so that one CTA (and one TMEM allocation) owns each SM
   const int smem = L::kBytes > 118 * 1024 ? L::kBytes : 118 * 1024;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // The opt-in shared-memory size is set once per device and instantiation,
+  // so later launches (including ones inside CUDA-graph capture) make no
+  // attribute calls.
+  static std::atomic<uint64_t> configured{0};
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
+  const uint64_t bit = device < 64 ? (uint64_t(1) << device) : 0;
+  if (bit == 0 || !(configured.load(std::memory_order_acquire) & bit)) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return err;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
   kernel<<<grid, L::kThreads, smem, stream>>>(prm);
   return cudaGetLastError();
 }

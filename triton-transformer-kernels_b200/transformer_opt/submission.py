@@ -6,6 +6,12 @@ same ``forward(x, valid_token_mask=None)``, same counters and the same
 state-dict surface, so the organizer harness's strict ``copy_model_weights``
 works unchanged).
 
+execution_mode: "eager" launches the fused forward op by op; "graph" captures
+it once per input signature into a CUDA graph and replays it (fresh input
+copied into the graph's static buffer, output cloned so results never alias,
+the reference's _InferenceGraph contract, submission.py:674-723); "auto"
+replays only launch-bound forwards (AUTO_GRAPH_MAX_ELEMENTS).
+
 On an sm_100 GPU in inference mode every layer runs
   packed QKV projection (cuBLAS, fp32) or three projections (16-bit)
   -> fused attention (libb200tk, tcgen05)  -> out_proj (cuBLAS)
@@ -45,7 +51,12 @@ from transformer_opt.model import (
     split_heads,
 )
 
-EXECUTION_MODES = ("auto", "eager")
+EXECUTION_MODES = ("auto", "eager", "graph")
+# "auto" replays a CUDA graph when the forward is launch-bound: at most this
+# many activation elements (batch * seq * d_model) times layers. Larger
+# forwards keep the GPU busy without one, and replay would add an input copy
+# and an output copy.
+AUTO_GRAPH_MAX_ELEMENTS = 1 << 22
 
 __all__ = ["TransformerConfig", "UserOptimizedTransformer"]
 
@@ -77,6 +88,7 @@ class UserOptimizedTransformer(TransformerWeights):
         }
         self.fused_residual_layer_norm_calls = 0
         self.cuda_graph_replays = 0
+        self._graph: Optional["_ForwardGraph"] = None
         # Derived, non-persistent inference data keyed by id(attention module):
         # (parameter signature, packed weight [3d, d], packed bias [3d]).
         self._packed_qkv_cache: Dict[int, Tuple[tuple, torch.Tensor, torch.Tensor]] = {}
@@ -91,6 +103,7 @@ class UserOptimizedTransformer(TransformerWeights):
         state = super().__getstate__().copy()
         state.pop("_lock", None)
         state["_packed_qkv_cache"] = {}
+        state["_graph"] = None
         return state
 
     def __setstate__(self, state):
@@ -98,9 +111,16 @@ class UserOptimizedTransformer(TransformerWeights):
         self._lock = threading.RLock()
 
     def _apply(self, fn, recurse=True):
-        # device / dtype moves invalidate the packed projection weights
+        # device / dtype moves invalidate the packed projection weights and
+        # release the captured graph (and its memory pool)
         self._packed_qkv_cache.clear()
+        self.clear_cuda_graph()
         return super()._apply(fn, recurse=recurse)
+
+    def clear_cuda_graph(self) -> None:
+        """Release the cached capture; a later eligible call captures again."""
+        with self._lock:
+            self._graph = None
 
     # ------------------------------------------------------------ projections
     @staticmethod
@@ -208,8 +228,55 @@ class UserOptimizedTransformer(TransformerWeights):
         reason = self.fused_route_reason(x, valid_token_mask)
         if reason is None:
             _native.load()  # on an eligible GPU a missing library is an error
+            if self._graph_eligible(x):
+                signature = self._graph_signature(x, valid_token_mask)
+                if signature is not None:
+                    return self._graph_forward(x, valid_token_mask, signature)
             return self._forward_fused(x, valid_token_mask)
         return self._forward_eager(x, valid_token_mask)
+
+    # ------------------------------------------------------------ CUDA graph
+    def _graph_eligible(self, x: torch.Tensor) -> bool:
+        if self.execution_mode == "eager" or torch.cuda.is_current_stream_capturing():
+            return False
+        if self.execution_mode == "graph":
+            return True
+        return x.numel() * len(self.layers) <= AUTO_GRAPH_MAX_ELEMENTS
+
+    def _graph_signature(self, x, valid_token_mask) -> Optional[tuple]:
+        """Everything a replay depends on, or None when it cannot be tracked."""
+        params = []
+        for module in self.modules():
+            if module.training or module._forward_hooks or module._forward_pre_hooks:
+                return None
+            for parameter in module._parameters.values():
+                if parameter is None:
+                    continue
+                if parameter.is_inference():
+                    return None  # no version counter: in-place updates would go unseen
+                params.append((parameter.data_ptr(), parameter._version))
+        norms = tuple(
+            m.eps for m in self.modules() if isinstance(m, nn.LayerNorm)
+        )
+        return (
+            tuple(params), norms, self.attention_backend, x.device, tuple(x.shape), x.dtype,
+            valid_token_mask is not None, torch.backends.cuda.matmul.allow_tf32,
+            torch.is_inference_mode_enabled(),  # static buffers are inference tensors or not
+        )
+
+    def _graph_forward(self, x, valid_token_mask, signature) -> torch.Tensor:
+        with self._lock:
+            graph = self._graph
+            if graph is None or graph.signature != signature:
+                self._graph = None
+                graph = _ForwardGraph(self, x, valid_token_mask, signature)
+                self._graph = graph
+            out = graph.replay(x, valid_token_mask)
+            for backend, count in graph.backend_counts.items():
+                self.attention_backend_counts[backend] += count
+            self.fused_residual_layer_norm_calls += graph.fused_calls
+            self.cuda_graph_replays += 1
+            return out
 
     # ----------------------------------------------------------------- fused
     def _fused_residual_norm(
@@ -269,3 +336,52 @@ class UserOptimizedTransformer(TransformerWeights):
         if valid_token_mask is not None:
             x = x.masked_fill(~valid_token_mask[..., None], 0)
         return x
+
+
+class _ForwardGraph:
+    """One captured fused forward with its own static input and output."""
+
+    def __init__(self, model, x, valid_token_mask, signature) -> None:
+        self.signature = signature
+        self.x = x.clone()
+        self.mask = valid_token_mask.clone() if valid_token_mask is not None else None
+        counts_before = dict(model.attention_backend_counts)
+        fused_before = model.fused_residual_layer_norm_calls
+        stream = torch.cuda.Stream(device=x.device)
+        current = torch.cuda.current_stream(x.device)
+        stream.wait_stream(current)
+        try:
+            with torch.cuda.stream(stream):
+                # warm-up outside capture: builds packed weights and resolves
+                # the library's per-device state
+                model._forward_fused(self.x, self.mask)
+            current.wait_stream(stream)
+            capture_counts = dict(model.attention_backend_counts)
+            capture_fused = model.fused_residual_layer_norm_calls
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=stream):
+                self.out = model._forward_fused(self.x, self.mask)
+            current.wait_stream(stream)
+            self.backend_counts = {
+                k: v - capture_counts[k] for k, v in model.attention_backend_counts.items()
+            }
+            self.fused_calls = model.fused_residual_layer_norm_calls - capture_fused
+            # keep the packed weights the graph reads alive
+            self.packed = tuple(model._packed_qkv_cache.values())
+            self.done = torch.cuda.Event()
+            self.done.record(current)
+        finally:
+            # warm-up and capture are set-up, not user-visible forwards
+            model.attention_backend_counts = counts_before
+            model.fused_residual_layer_norm_calls = fused_before
+
+    def replay(self, x, valid_token_mask) -> torch.Tensor:
+        current = torch.cuda.current_stream(x.device)
+        current.wait_event(self.done)
+        self.x.copy_(x)
+        if self.mask is not None:
+            self.mask.copy_(valid_token_mask)
+        self.graph.replay()
+        out = self.out.clone()  # later replays must not overwrite a returned result
+        self.done.record(current)
+        return out
