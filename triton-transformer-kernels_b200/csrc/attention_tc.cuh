@@ -459,33 +459,46 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
     }
   } else if (warp == L::kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kFmt = ElemTraits<T>::kFmt;
-      constexpr uint32_t idesc_qk = make_idesc(kFmt, 0, 0, BN, BM);  // Q K-major, K K-major
-      constexpr uint32_t idesc_pv = make_idesc(kFmt, 0, 1, D, BM);   // P (tmem), V MN-major
-      bool ok = true;
-      int kc = 0, vc = 0;
-      for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
-        const Item w = item_at(it);
-        auto in_pass2 = [&](int g) { return !kTwoPass || g >= w.n_kv; };
-        auto tile_of = [&](int g) { return (kTwoPass && g >= w.n_kv) ? g - w.n_kv : g; };
-        ok = wait(kSplit ? bar_q_ready : bar_q_full, k & 1);
-        if (!ok) break;
-        tc_fence_after();
+    // The whole warp walks the schedule, so loop control and descriptor
+    // arithmetic stay warp-uniform; one elected lane issues every
+    // tcgen05.mma and every tcgen05.commit (a commit tracks the MMAs of the
+    // thread that issues it). Shared-memory descriptors are built once and
+    // advanced by adding byte offsets >> 4 to their address field (all
+    // offsets are compile-time constants per K step).
+    const bool leader = elect_one_sync();
+    constexpr uint32_t kFmt = ElemTraits<T>::kFmt;
+    constexpr uint32_t idesc_qk = make_idesc(kFmt, 0, 0, BN, BM);  // Q K-major, K K-major
+    constexpr uint32_t idesc_pv = make_idesc(kFmt, 0, 1, D, BM);   // P (tmem), V MN-major
+    const uint64_t q_desc0 = make_sdesc(sbase + L::kQ, 16, 1024, kLayoutSw128);
+    const uint64_t k_desc0 = make_sdesc(sbase + L::kK, 16, 1024, kLayoutSw128);
+    const uint64_t v_desc0 = make_sdesc(sbase + L::kV, BN * 128, L::kVSbo, L::kVLayout);
+    auto wait_all = [&](uint32_t bar, uint32_t parity) {
+      return __all_sync(0xFFFFFFFFu, wait(bar, parity));
+    };
+    bool ok = true;
+    int kc = 0, vc = 0;
+    for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+      const Item w = item_at(it);
+      auto in_pass2 = [&](int g) { return !kTwoPass || g >= w.n_kv; };
+      auto tile_of = [&](int g) { return (kTwoPass && g >= w.n_kv) ? g - w.n_kv : g; };
+      ok = wait_all(kSplit ? bar_q_ready : bar_q_full, k & 1);
+      if (!ok) break;
+      tc_fence_after();
 
-        // S_t(g) = Q_t K_g^T into score buffer (kc + g) % NSB of query tile
-        // t. The K tile is waited for by the first query tile and released
-        // after the last; after the item's last score MMA, Q is released.
-        auto issue_s = [&](int t, int g) -> bool {
-          const int kg = kc + g;
-          const int s = kg % KST;
-          if (t == 0) {
-            if (!wait(kSplit ? bar_k_ready(s) : bar_k_full(s), (kg / KST) & 1)) return false;
-            tc_fence_after();
-          }
+      // S_t(g) = Q_t K_g^T into score buffer (kc + g) % NSB of query tile
+      // t. The K tile is waited for by the first query tile and released
+      // after the last; after the item's last score MMA, Q is released.
+      auto issue_s = [&](int t, int g) -> bool {
+        const int kg = kc + g;
+        const int s = kg % KST;
+        if (t == 0) {
+          if (!wait_all(kSplit ? bar_k_ready(s) : bar_k_full(s), (kg / KST) & 1)) return false;
+          tc_fence_after();
+        }
+        if (leader) {
           const uint32_t d_tmem = tmem + L::t_s(t, kg % NSB);
-          const uint32_t qa = sbase + L::kQ + t * L::kQStage;
-          const uint32_t kb = sbase + L::kK + s * L::kKStage;
+          const uint64_t qd = q_desc0 + static_cast<uint32_t>((t * L::kQStage) >> 4);
+          const uint64_t kd = k_desc0 + static_cast<uint32_t>((s * L::kKStage) >> 4);
           constexpr int kSteps = D / L::kUmmaK;
           constexpr int kPasses = kSplit ? 3 : 1;
 #pragma unroll
@@ -494,20 +507,19 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             // comes from TMEM (hi / lo columns written by the split warps),
             // so the only smem operand of the score MMA is K.
             const uint32_t q_tmem = tmem + (pass == 0 ? L::t_qlo(t) : L::t_qhi(t));
-            const uint32_t b_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
+            const int b_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
             for (int ks = 0; ks < kSteps; ++ks) {
-              const int byte = ks * 32;
-              const int atom = byte / 128;
-              const int within = byte % 128;
+              constexpr int kAtomStep = 128 / 32;  // K steps per 128-byte swizzle row
+              const int atom = ks / kAtomStep;
+              const int within = (ks % kAtomStep) * 32;
               const uint64_t bdesc =
-                  make_sdesc(kb + b_off + atom * BN * 128 + within, 16, 1024, kLayoutSw128);
+                  kd + static_cast<uint32_t>((b_off + atom * BN * 128 + within) >> 4);
               if constexpr (kSplit) {
                 mma_ts_tf32(d_tmem, q_tmem + ks * 8, bdesc, idesc_qk,
                             (pass > 0 || ks > 0) ? 1u : 0u);
               } else {
-                const uint64_t adesc =
-                    make_sdesc(qa + atom * BM * 128 + within, 16, 1024, kLayoutSw128);
+                const uint64_t adesc = qd + static_cast<uint32_t>((atom * BM * 128 + within) >> 4);
                 mma_ss_f16(d_tmem, adesc, bdesc, idesc_qk, ks > 0 ? 1u : 0u);
               }
             }
@@ -517,33 +529,36 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             if (g == w.n_s - 1) tc_commit(bar_q_empty);
           }
           tc_commit(bar_s_full(t, kg % NSB));
-          return true;
-        };
+        }
+        __syncwarp();
+        return true;
+      };
 
-        for (int g = 0; g < NSB && g < w.n_s && ok; ++g)
-          for (int t = 0; t < NQ && ok; ++t) ok = issue_s(t, g);
-        for (int g = 0; g < w.n_s && ok; ++g) {
-          for (int t = 0; t < NQ && ok; ++t) {
-            // the softmax warps of tile t are done with S_t(g) (and wrote P_t(g))
-            ok = wait(bar_p_full(t), (kc + g) & 1);
-            if (!ok) break;
-            if (in_pass2(g)) {
-              const int j = tile_of(g);
-              const int vg = vc + j;
-              const int sv = vg % VST;
-              if (t == 0) {
-                ok = wait(kSplit ? bar_v_ready(sv) : bar_v_full(sv), (vg / VST) & 1);
-                if (!ok) break;
-              }
-              // the first P@V of an item overwrites O: the previous item's
-              // epilogue must have read it
-              if (j == 0 && k > 0) {
-                ok = wait(bar_o_empty(t), (k - 1) & 1);
-                if (!ok) break;
-              }
-              tc_fence_after();
+      for (int g = 0; g < NSB && g < w.n_s && ok; ++g)
+        for (int t = 0; t < NQ && ok; ++t) ok = issue_s(t, g);
+      for (int g = 0; g < w.n_s && ok; ++g) {
+        for (int t = 0; t < NQ && ok; ++t) {
+          // the softmax warps of tile t are done with S_t(g) (and wrote P_t(g))
+          ok = wait_all(bar_p_full(t), (kc + g) & 1);
+          if (!ok) break;
+          if (in_pass2(g)) {
+            const int j = tile_of(g);
+            const int vg = vc + j;
+            const int sv = vg % VST;
+            if (t == 0) {
+              ok = wait_all(kSplit ? bar_v_ready(sv) : bar_v_full(sv), (vg / VST) & 1);
+              if (!ok) break;
+            }
+            // the first P@V of an item overwrites O: the previous item's
+            // epilogue must have read it
+            if (j == 0 && k > 0) {
+              ok = wait_all(bar_o_empty(t), (k - 1) & 1);
+              if (!ok) break;
+            }
+            tc_fence_after();
+            if (leader) {
               const uint32_t o_tmem = tmem + L::t_o(t);
-              const uint32_t vbuf = sbase + L::kV + sv * L::kVStage;
+              const uint64_t vd = v_desc0 + static_cast<uint32_t>((sv * L::kVStage) >> 4);
               constexpr int kSteps = BN / L::kUmmaK;
               constexpr int kPasses = kSplit ? 3 : 1;
 #pragma unroll
@@ -551,13 +566,13 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
                 const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, (kc + g) % NSB)
                                         : pass == 0 ? tmem + L::t_plo(t)
                                                     : tmem + L::t_phi(t);
-                const uint32_t v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
+                const int v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
                 for (int ks = 0; ks < kSteps; ++ks) {
                   // V is MN-major: K advances over 128-byte rows; LBO steps
                   // across head_dim atoms, SBO across the swizzle's row groups.
-                  const uint64_t bdesc = make_sdesc(vbuf + v_off + ks * L::kUmmaK * 128,
-                                                    BN * 128, L::kVSbo, L::kVLayout);
+                  const uint64_t bdesc =
+                      vd + static_cast<uint32_t>((v_off + ks * L::kUmmaK * 128) >> 4);
                   const uint32_t a_tmem = p_tmem + ks * 8;  // 8 columns per K step
                   const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
                   if constexpr (kSplit)
@@ -569,18 +584,22 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
               tc_commit(bar_pv_done(t));
               if (t == NQ - 1) tc_commit(bar_v_empty(sv));
             }
-            if (g + NSB < w.n_s) ok = issue_s(t, g + NSB);
+            __syncwarp();
           }
+          if (g + NSB < w.n_s) ok = issue_s(t, g + NSB);
         }
-        kc += w.n_s;
-        vc += w.n_kv;
       }
-      // make sure no MMA is still writing TMEM when the CTA tears down
+      kc += w.n_s;
+      vc += w.n_kv;
+    }
+    // make sure no MMA is still writing TMEM when the CTA tears down
+    if (leader) {
       tc_commit(bar_drain);
       uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(bar_drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
       }
     }
+    __syncwarp();
   } else if (kSplit && warp >= L::kSplitWarp0) {
     // ------------------------------------------- fp32 hi/lo split workers
     // The tf32 MMA reads the top 19 bits of each fp32 operand and ignores the
