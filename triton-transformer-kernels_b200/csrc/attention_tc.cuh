@@ -182,7 +182,10 @@ __device__ __forceinline__ uint32_t pack_pair(float a, float b) {
 template <typename T, int D, int BN, int KST, int VST, int NQ>
 struct TcLayout {
   static constexpr bool kSplit = ElemTraits<T>::kSplit;
-  static constexpr int kNSB = NQ == 1 ? 2 : 1;    // score buffers per query tile
+  // Score buffers per query tile: two whenever TMEM holds them (the next
+  // score MMA then overlaps the softmax of the current tile), else one.
+  static constexpr int kNSB =
+      (NQ * (ElemTraits<T>::kSplit ? 2 * BN + 2 * BN + 3 * D : 2 * BN + D)) <= 512 ? 2 : 1;
   static constexpr int kElem = sizeof(T);
   static constexpr int kAtomElems = 128 / kElem;  // elements per 128-byte row
   static constexpr int kAtoms = D / kAtomElems;   // swizzle atoms along head_dim
@@ -205,12 +208,14 @@ struct TcLayout {
   static constexpr int kSoftmaxWarps = NQ * kSoftmaxWarpsPerTile;
   static constexpr int kStats = kV + VST * kVStage;  // (max, sum) exchange, float2 per thread
   static constexpr int kBar = kStats + NQ * kThreadsPerRow * BM * 8;
-  static constexpr int kNumBars = 2 + 3 * KST + 3 * VST + NQ * kNSB + 4 * NQ + 2;
+  static constexpr int kNumBars = 2 + 3 * KST + 3 * VST + 2 * NQ * kNSB + 3 * NQ + 2;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 64 + 1024;  // + alignment slack
   // TMEM columns per query tile: S buffers, O, and for fp32 one P hi and one
   // P lo buffer plus the Q hi / Q lo operands of the score MMA. 16-bit P
-  // (packed pairs) overwrites the first BN/2 columns of its S buffer.
+  // (packed pairs) goes back into the score buffer it came from: each
+  // half-row thread packs its BN/2 keys into the first BN/4 columns of its
+  // own half, so no thread overwrites scores another thread has yet to read.
   static constexpr int kTileCols = kSplit ? kNSB * BN + 2 * BN + 3 * D : kNSB * BN + D;
   static constexpr int kTCols = NQ * kTileCols;
   static constexpr uint32_t kTAlloc = kTCols <= 32    ? 32
@@ -271,12 +276,17 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
   auto bar_v_ready = [&](int s) { return vb + 8 * (VST + s); };
   auto bar_v_empty = [&](int s) { return vb + 8 * (2 * VST + s); };
   const uint32_t tb = vb + 8 * 3 * VST;
+  // One s_full and one p_full barrier per score buffer: the softmax warps
+  // arrive on a buffer's p_full again only after the MMA warp has consumed
+  // its previous phase (the next score tile of that buffer is issued after
+  // it), so no parity phase can be skipped.
   auto bar_s_full = [&](int t, int buf) { return tb + 8 * (t * NSB + buf); };
-  auto bar_p_full = [&](int t) { return tb + 8 * (NQ * NSB + t); };
-  auto bar_pv_done = [&](int t) { return tb + 8 * (NQ * NSB + NQ + t); };
-  auto bar_stats = [&](int t) { return tb + 8 * (NQ * NSB + 2 * NQ + t); };
-  auto bar_o_empty = [&](int t) { return tb + 8 * (NQ * NSB + 3 * NQ + t); };
-  const uint32_t bar_q_empty = tb + 8 * (NQ * NSB + 4 * NQ);
+  auto bar_p_full = [&](int t, int buf) { return tb + 8 * (NQ * NSB + t * NSB + buf); };
+  const uint32_t tb2 = tb + 8 * (2 * NQ * NSB);
+  auto bar_pv_done = [&](int t) { return tb2 + 8 * t; };
+  auto bar_stats = [&](int t) { return tb2 + 8 * (NQ + t); };
+  auto bar_o_empty = [&](int t) { return tb2 + 8 * (2 * NQ + t); };
+  const uint32_t bar_q_empty = tb2 + 8 * (3 * NQ);
   const uint32_t bar_drain = bar_q_empty + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
@@ -299,8 +309,10 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       mbar_init(bar_v_empty(s), 1);
     }
     for (int t = 0; t < NQ; ++t) {
-      for (int bf = 0; bf < NSB; ++bf) mbar_init(bar_s_full(t, bf), 1);
-      mbar_init(bar_p_full(t), 128 * L::kThreadsPerRow);
+      for (int bf = 0; bf < NSB; ++bf) {
+        mbar_init(bar_s_full(t, bf), 1);
+        mbar_init(bar_p_full(t, bf), 128 * L::kThreadsPerRow);
+      }
       mbar_init(bar_pv_done(t), 1);
       mbar_init(bar_stats(t), 128 * L::kThreadsPerRow);
       mbar_init(bar_o_empty(t), 128 * L::kThreadsPerRow);
@@ -539,7 +551,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       for (int g = 0; g < w.n_s && ok; ++g) {
         for (int t = 0; t < NQ && ok; ++t) {
           // the softmax warps of tile t are done with S_t(g) (and wrote P_t(g))
-          ok = wait_all(bar_p_full(t), (kc + g) & 1);
+          ok = wait_all(bar_p_full(t, (kc + g) % NSB), ((kc + g) / NSB) & 1);
           if (!ok) break;
           if (in_pass2(g)) {
             const int j = tile_of(g);
@@ -573,7 +585,13 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
                   // across head_dim atoms, SBO across the swizzle's row groups.
                   const uint64_t bdesc =
                       vd + static_cast<uint32_t>((v_off + ks * L::kUmmaK * 128) >> 4);
-                  const uint32_t a_tmem = p_tmem + ks * 8;  // 8 columns per K step
+                  // 8 columns per K step. 16-bit P: each half-row thread
+                  // packs its BN/2 keys into the first BN/4 columns of its
+                  // own half of the score buffer.
+                  constexpr int kStepsPerHalf = BN / 2 / L::kUmmaK;
+                  const uint32_t a_tmem =
+                      kSplit ? p_tmem + ks * 8
+                             : p_tmem + (ks / kStepsPerHalf) * (BN / 2) + (ks % kStepsPerHalf) * 8;
                   const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
                   if constexpr (kSplit)
                     mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
@@ -737,7 +755,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             // pass 1 keeps nothing in TMEM: the score buffer is free as soon
             // as it has been read, so the next score tile overlaps this math.
             tc_fence_before();
-            mbar_arrive(bar_p_full(t));
+            mbar_arrive(bar_p_full(t, buf));
           }
           const bool masked =
               HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
@@ -847,9 +865,9 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             pk[i / 2] = cvt_pack2<T>(a, c);
           }
           if (j > 0) {
-            // PV_{j-1} must have read P_{j-1} (same TMEM columns). Waiting
-            // for every P@V phase in order also keeps the pv_done parity
-            // barrier at most one phase ahead of this wait.
+            // Waiting for every P@V phase in order keeps the pv_done parity
+            // barrier at most one phase ahead of this wait (and, with one
+            // score buffer, PV_{j-1} has read P_{j-1} from these columns).
             if (!__all_sync(0xFFFFFFFFu, wait(bar_pv_done(t), (vc + j - 1) & 1))) {
               ok = false;
               break;
@@ -857,14 +875,14 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           }
 #pragma unroll
           for (int c = 0; c < HB / 64; ++c)
-            tmem_st32(tmem + lane_off + L::t_s(t, buf) + c0 / 2 + c * 32,
+            tmem_st32(tmem + lane_off + L::t_s(t, buf) + c0 + c * 32,
                       *reinterpret_cast<const uint32_t(*)[32]>(&pk[c * 32]));
           if constexpr (HB % 64 != 0)
-            tmem_st16(tmem + lane_off + L::t_s(t, buf) + c0 / 2 + (HB / 64) * 32,
+            tmem_st16(tmem + lane_off + L::t_s(t, buf) + c0 + (HB / 64) * 32,
                       &pk[(HB / 64) * 32]);
           tc_wait_st();
           tc_fence_before();
-          mbar_arrive(bar_p_full(t));
+          mbar_arrive(bar_p_full(t, buf));
         }
 
         // epilogue: this thread stores head_dim columns [half*D/2, (half+1)*D/2)
@@ -1042,7 +1060,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           }
           tc_wait_st();
           tc_fence_before();
-          mbar_arrive(bar_p_full(0));
+          mbar_arrive(bar_p_full(0, buf));
         }
 
         // epilogue: combine the two partial row sums, store this half of O
