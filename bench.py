@@ -25,6 +25,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import select
 import statistics
 import subprocess
 import sys
@@ -51,8 +52,11 @@ L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 # DRAM bytes per attention launch (dram__bytes_read.sum + dram__bytes_write.sum)
 # from one ncu capture of the same kernel and workload; see profiles/.
 NCU_ATTENTION_TRAFFIC = {
-    # profiles/attention_fwd_tc_fp32_C2.md: 201.4 MB read + 49.5 MB written
-    "C2": 250.9e6,
+    # profiles/attention_fwd_tc_fp32_C2.md: 201.5 MB read + 49.5 MB written
+    "C2": 251.0e6,
+    # profiles/attention_fwd_tc_bf16_C3.md: captured at batch 1 (406.3 MB read
+    # + 121.6 MB written), scaled by C3's 4 independent sequences
+    "C3": 4 * 527.9e6,
 }
 
 
@@ -98,6 +102,7 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        self.lines = []
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
@@ -106,10 +111,28 @@ class ClockSampler:
             )
         except (OSError, ValueError):
             self.proc = None
+        if self.proc is not None:
+            # sampling is live before the timed work starts: the first sample
+            # is taken on entry (a timed region can be shorter than the period)
+            ready, _, _ = select.select([self.proc.stdout], [], [], 10.0)
+            if ready:
+                first = self.proc.stdout.readline()
+                if first.strip():
+                    self.lines.append(first.strip())
         return self
 
+    def _query_once(self) -> None:
+        try:
+            out = subprocess.run(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits"],
+                capture_output=True, text=True, timeout=20,
+            ).stdout
+            self.lines += [ln for ln in out.splitlines() if ln.strip()]
+        except (OSError, subprocess.SubprocessError):
+            pass
+
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -117,7 +140,9 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            self.lines += [ln for ln in out.splitlines() if ln.strip()]
+            if len(self.lines) < 2:
+                self._query_once()  # the region ended before the next periodic sample
 
     def summary(self) -> dict:
         sm, sm_max, reasons = [], None, set()
@@ -453,7 +478,7 @@ def run_b200_arm(args) -> int:
         "unit": "TFLOP/s",
         "frac": achieved_tflops / peak_tf,
         "peak_source": f"{peaks['source']} bf16_tflops_sustained",
-        "traffic": NCU_ATTENTION_TRAFFIC.get(name),
+        "traffic": NCU_ATTENTION_TRAFFIC.get(name) if args.batch is None else None,
         "flops_per_launch": flops,
         "launch_ms": attn_ms,
     }
@@ -533,6 +558,8 @@ def main() -> int:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--config", choices=sorted(CONFIGS), default="C2")
+    parser.add_argument("--batch", type=int, default=None,
+                        help="override the configuration's batch per GPU (profiling runs)")
     parser.add_argument("--execution-mode", choices=("auto", "eager", "graph"), default="auto",
                         help="UserOptimizedTransformer execution_mode")
     parser.add_argument("--no-validate", dest="validate", action="store_false")
@@ -542,6 +569,10 @@ def main() -> int:
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         parser.error("--warmup must be >= 3")
+    if args.batch is not None:
+        if args.batch < 1:
+            parser.error("--batch must be >= 1")
+        CONFIGS[args.config] = (args.batch,) + tuple(CONFIGS[args.config][1:])
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_b200_arm(args)
