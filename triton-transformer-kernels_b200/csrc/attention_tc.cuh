@@ -233,11 +233,13 @@ struct TcLayout {
   }
   __host__ __device__ static constexpr int t_qhi(int t) { return t_o(t) + D; }
   __host__ __device__ static constexpr int t_qlo(int t) { return t_o(t) + 2 * D; }
-  // warps: [softmax][producer][MMA][fp32: split x 4]
+  // warps: [softmax][producer][MMA issuers][fp32: split x 4]. 16-bit: one
+  // MMA warp for all query tiles; fp32: one for the score MMAs, one for P@V.
+  static constexpr int kMmaWarps = kSplit ? 2 : 1;
   static constexpr int kProducerWarp = kSoftmaxWarps;
   static constexpr int kMmaWarp = kSoftmaxWarps + 1;
-  static constexpr int kSplitWarp0 = kSoftmaxWarps + 2;
-  static constexpr int kThreads = 32 * (kSoftmaxWarps + 2 + (kSplit ? 4 : 0));
+  static constexpr int kSplitWarp0 = kMmaWarp + kMmaWarps;
+  static constexpr int kThreads = 32 * (kSplitWarp0 + (kSplit ? 4 : 0));
   // V (MN-major B operand of P@V): 16-bit types use the 128-byte swizzle
   // (8-row groups, SBO 1024 B); tf32 requires the 128B_BASE32B swizzle
   // (32-byte chunks, 4-row groups, SBO 512 B), loaded by TMA with
@@ -318,7 +320,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       mbar_init(bar_o_empty(t), 128 * L::kThreadsPerRow);
     }
     mbar_init(bar_q_empty, 1);
-    mbar_init(bar_drain, 1);
+    mbar_init(bar_drain, L::kMmaWarps);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -469,14 +471,22 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           }
       }
     }
-  } else if (warp == L::kMmaWarp) {
-    // ---------------------------------------------------------- MMA issuer
-    // The whole warp walks the schedule, so loop control and descriptor
-    // arithmetic stay warp-uniform; one elected lane issues every
-    // tcgen05.mma and every tcgen05.commit (a commit tracks the MMAs of the
-    // thread that issues it). Shared-memory descriptors are built once and
-    // advanced by adding byte offsets >> 4 to their address field (all
-    // offsets are compile-time constants per K step).
+  } else if (warp >= L::kMmaWarp && warp < L::kMmaWarp + L::kMmaWarps) {
+    // --------------------------------------------------------- MMA issuers
+    // 16-bit: one warp issues the score and P@V MMAs of all query tiles (P
+    // aliases the score buffer, so a tile's P@V and its next score MMA keep
+    // one issue order; interleaving the tiles in one warp also measured
+    // faster than a warp per tile). fp32 (one query tile): warp 0 issues the
+    // score MMAs, warp 1 the P@V MMAs; P has TMEM buffers of its own, so the
+    // two streams only meet through the softmax barriers.
+    //
+    // Each warp walks its schedule warp-uniformly (loop control and
+    // descriptor arithmetic stay uniform); one elected lane issues every
+    // tcgen05.mma and tcgen05.commit (a commit tracks the MMAs of the thread
+    // that issues it). Shared-memory descriptors are built once and advanced
+    // by adding byte offsets >> 4 to their address field (compile-time
+    // constants per K step).
+    const bool do_s = !kSplit || warp == L::kMmaWarp;
     const bool leader = elect_one_sync();
     constexpr uint32_t kFmt = ElemTraits<T>::kFmt;
     constexpr uint32_t idesc_qk = make_idesc(kFmt, 0, 0, BN, BM);  // Q K-major, K K-major
@@ -491,15 +501,16 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
     int kc = 0, vc = 0;
     for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
       const Item w = item_at(it);
-      auto in_pass2 = [&](int g) { return !kTwoPass || g >= w.n_kv; };
       auto tile_of = [&](int g) { return (kTwoPass && g >= w.n_kv) ? g - w.n_kv : g; };
-      ok = wait_all(kSplit ? bar_q_ready : bar_q_full, k & 1);
-      if (!ok) break;
-      tc_fence_after();
+      if (do_s) {
+        ok = wait_all(kSplit ? bar_q_ready : bar_q_full, k & 1);
+        if (!ok) break;
+        tc_fence_after();
+      }
 
-      // S_t(g) = Q_t K_g^T into score buffer (kc + g) % NSB of query tile
-      // t. The K tile is waited for by the first query tile and released
-      // after the last; after the item's last score MMA, Q is released.
+      // S_t(g) = Q_t K_g^T into score buffer (kc + g) % NSB of tile t. The K
+      // tile is waited for by the first query tile and released after the
+      // last; after the item's last score MMA, Q is released.
       auto issue_s = [&](int t, int g) -> bool {
         const int kg = kc + g;
         const int s = kg % KST;
@@ -546,65 +557,86 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         return true;
       };
 
-      for (int g = 0; g < NSB && g < w.n_s && ok; ++g)
-        for (int t = 0; t < NQ && ok; ++t) ok = issue_s(t, g);
-      for (int g = 0; g < w.n_s && ok; ++g) {
-        for (int t = 0; t < NQ && ok; ++t) {
-          // the softmax warps of tile t are done with S_t(g) (and wrote P_t(g))
-          ok = wait_all(bar_p_full(t, (kc + g) % NSB), ((kc + g) / NSB) & 1);
-          if (!ok) break;
-          if (in_pass2(g)) {
-            const int j = tile_of(g);
-            const int vg = vc + j;
-            const int sv = vg % VST;
-            if (t == 0) {
-              ok = wait_all(kSplit ? bar_v_ready(sv) : bar_v_full(sv), (vg / VST) & 1);
-              if (!ok) break;
-            }
-            // the first P@V of an item overwrites O: the previous item's
-            // epilogue must have read it
-            if (j == 0 && k > 0) {
-              ok = wait_all(bar_o_empty(t), (k - 1) & 1);
-              if (!ok) break;
-            }
-            tc_fence_after();
-            if (leader) {
-              const uint32_t o_tmem = tmem + L::t_o(t);
-              const uint64_t vd = v_desc0 + static_cast<uint32_t>((sv * L::kVStage) >> 4);
-              constexpr int kSteps = BN / L::kUmmaK;
-              constexpr int kPasses = kSplit ? 3 : 1;
+      // O_t += P_t(g) V_j for pass-2 step g (key tile j). The V tile is
+      // waited for by the first query tile and released after the last.
+      auto issue_pv = [&](int t, int g) -> bool {
+        const int j = tile_of(g);
+        const int vg = vc + j;
+        const int sv = vg % VST;
+        if (t == 0 &&
+            !wait_all(kSplit ? bar_v_ready(sv) : bar_v_full(sv), (vg / VST) & 1))
+          return false;
+        // the first P@V of an item overwrites O: the previous item's
+        // epilogue must have read it
+        if (j == 0 && k > 0 && !wait_all(bar_o_empty(t), (k - 1) & 1)) return false;
+        tc_fence_after();
+        if (leader) {
+          const uint32_t o_tmem = tmem + L::t_o(t);
+          const uint64_t vd = v_desc0 + static_cast<uint32_t>((sv * L::kVStage) >> 4);
+          constexpr int kSteps = BN / L::kUmmaK;
+          constexpr int kPasses = kSplit ? 3 : 1;
 #pragma unroll
-              for (int pass = 0; pass < kPasses; ++pass) {
-                const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, (kc + g) % NSB)
-                                        : pass == 0 ? tmem + L::t_plo(t)
-                                                    : tmem + L::t_phi(t);
-                const int v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
+          for (int pass = 0; pass < kPasses; ++pass) {
+            const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, (kc + g) % NSB)
+                                    : pass == 0 ? tmem + L::t_plo(t)
+                                                : tmem + L::t_phi(t);
+            const int v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
-                for (int ks = 0; ks < kSteps; ++ks) {
-                  // V is MN-major: K advances over 128-byte rows; LBO steps
-                  // across head_dim atoms, SBO across the swizzle's row groups.
-                  const uint64_t bdesc =
-                      vd + static_cast<uint32_t>((v_off + ks * L::kUmmaK * 128) >> 4);
-                  // 8 columns per K step. 16-bit P: each half-row thread
-                  // packs its BN/2 keys into the first BN/4 columns of its
-                  // own half of the score buffer.
-                  constexpr int kStepsPerHalf = BN / 2 / L::kUmmaK;
-                  const uint32_t a_tmem =
-                      kSplit ? p_tmem + ks * 8
-                             : p_tmem + (ks / kStepsPerHalf) * (BN / 2) + (ks % kStepsPerHalf) * 8;
-                  const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
-                  if constexpr (kSplit)
-                    mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
-                  else
-                    mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
-                }
-              }
-              tc_commit(bar_pv_done(t));
-              if (t == NQ - 1) tc_commit(bar_v_empty(sv));
+            for (int ks = 0; ks < kSteps; ++ks) {
+              // V is MN-major: K advances over 128-byte rows; LBO steps
+              // across head_dim atoms, SBO across the swizzle's row groups.
+              const uint64_t bdesc =
+                  vd + static_cast<uint32_t>((v_off + ks * L::kUmmaK * 128) >> 4);
+              // 8 columns per K step. 16-bit P: each half-row thread packs
+              // its BN/2 keys into the first BN/4 columns of its own half of
+              // the score buffer.
+              constexpr int kStepsPerHalf = BN / 2 / L::kUmmaK;
+              const uint32_t a_tmem =
+                  kSplit ? p_tmem + ks * 8
+                         : p_tmem + (ks / kStepsPerHalf) * (BN / 2) + (ks % kStepsPerHalf) * 8;
+              const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
+              if constexpr (kSplit)
+                mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
+              else
+                mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
             }
-            __syncwarp();
           }
-          if (g + NSB < w.n_s) ok = issue_s(t, g + NSB);
+          tc_commit(bar_pv_done(t));
+          if (t == NQ - 1) tc_commit(bar_v_empty(sv));
+        }
+        __syncwarp();
+        return true;
+      };
+      // the softmax warps of tile t are done with S_t(g) (and wrote P_t(g))
+      auto wait_p = [&](int t, int g) {
+        return wait_all(bar_p_full(t, (kc + g) % NSB), ((kc + g) / NSB) & 1);
+      };
+
+      if constexpr (kSplit) {
+        if (do_s) {
+          // a score buffer is reused once the softmax has read it; steps
+          // count across items, so every phase of every buffer is waited
+          // for in order (the first tiles of an item reuse the buffers of
+          // the previous item's last tiles)
+          for (int g = 0; g < w.n_s && ok; ++g) {
+            if (kc + g >= NSB) ok = wait_p(0, g - NSB);
+            if (ok) ok = issue_s(0, g);
+          }
+        } else {
+          for (int g = 0; g < w.n_s && ok; ++g) {
+            ok = wait_p(0, g);
+            if (ok) ok = issue_pv(0, g);
+          }
+        }
+      } else {
+        for (int g = 0; g < NSB && g < w.n_s && ok; ++g)
+          for (int t = 0; t < NQ && ok; ++t) ok = issue_s(t, g);
+        for (int g = 0; g < w.n_s && ok; ++g) {
+          for (int t = 0; t < NQ && ok; ++t) {
+            ok = wait_p(t, g);
+            if (ok && g >= w.n_kv) ok = issue_pv(t, g);
+            if (ok && g + NSB < w.n_s) ok = issue_s(t, g + NSB);
+          }
         }
       }
       kc += w.n_s;
