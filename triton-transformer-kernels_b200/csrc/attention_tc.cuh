@@ -1,31 +1,40 @@
 // attention_tc.cuh - fused attention forward on sm_100a tensor cores.
 //
-// One CTA owns NQ (1 or 2) 128-row query tiles of one (batch, head) and walks
-// the key / value tiles of that head (the algorithm of the reference kernel
-// transformer_opt/kernels/attention.py:103-265):
-//   * producer warp : TMA loads of the Q tiles once and of K/V tiles into
-//                     KST/VST-deep smem rings (128-byte swizzle), shared by
-//                     all query tiles of the CTA.
-//   * MMA warp      : one elected thread issues tcgen05.mma: S_t = Q_t K_j^T
+// A CTA owns work items of NQ (1 or 2) 128-row query tiles of one (batch,
+// head) and walks the key / value tiles of that head (the algorithm of the
+// reference kernel transformer_opt/kernels/attention.py:103-265):
+//   * producer warp : TMA loads of the Q tiles and of K/V tiles into KST/VST
+//                     deep smem rings (128-byte swizzle), shared by all query
+//                     tiles of the CTA; the K and V rings are refilled
+//                     independently.
+//   * MMA warp(s)   : one elected lane issues tcgen05.mma: S_t = Q_t K_j^T
 //                     into TMEM score buffers, then O_t += P_t V_j with P read
-//                     from TMEM. With two query tiles each has one score
-//                     buffer, so tile 0's softmax overlaps tile 1's MMAs and
-//                     vice versa; with one tile the score buffer is doubled.
-//   * softmax warps : warpgroup t (4 warps) owns query tile t; thread r owns
-//                     row r (TMEM lane r). It reads S with tcgen05.ld,
-//                     reproduces the reference's dtype boundaries, masks
-//                     (causal diagonal, sequence end, key padding), keeps the
-//                     row max / sum in fp32, writes P back into TMEM and
-//                     finally stores the normalised output row.
-//   * split warps   : (fp32 only) split every fp32 tile in smem into a tf32
-//                     "hi" part (in place) and the residual "lo" part, so each
-//                     product runs as lo*hi + hi*lo + hi*hi (3xTF32).
-// Causal key tiles beyond the CTA's last query row are never loaded (the key
+//                     from TMEM. 16-bit: one warp for both query tiles (each
+//                     tile has one score buffer, so tile 0's softmax overlaps
+//                     tile 1's MMAs and vice versa). fp32: one warp issues the
+//                     score MMAs and another the P@V MMAs.
+//   * softmax warps : eight per query tile, two threads per score row (TMEM
+//                     lane r), each owning half of the key columns. They read
+//                     S with tcgen05.ld, reproduce the reference's dtype
+//                     boundaries, mask (causal diagonal, sequence end, key
+//                     padding), keep the row max / sum in fp32, write P back
+//                     into TMEM and finally store the normalised output row.
+//                     16-bit inputs take two passes over the keys (row max
+//                     and sum, then normalised P rounded to T); fp32 takes one
+//                     online pass on 3xTF32.
+//   * split warps   : (fp32 only) write the residual lo = x - tf32(x) of
+//                     every K/V tile (the tf32 MMA truncates the raw tile to
+//                     its hi part) and move Q hi / lo into TMEM once per item,
+//                     so each product runs as lo*hi + hi*lo + hi*hi.
+// Causal key tiles beyond the item's last query row are never loaded (the key
 // loop ends at min(S, last row + 1)), the reference's end bound (:163-166).
+// Non-causal launches are persistent (one CTA per SM walking the items).
 //
 // Every mbarrier wait is bounded (ptx_sm100.cuh mbar_wait): on timeout the
 // CTA raises an abort flag and a device status bit, drains its own copies and
-// MMAs with further bounded waits, frees TMEM and returns.
+// MMAs with further bounded waits, frees TMEM and returns. Parity barriers
+// only tell the current phase from the previous one, so every waiter observes
+// every phase of the barriers it waits on, in order.
 
 #pragma once
 
@@ -208,15 +217,28 @@ struct TcLayout {
   static constexpr int kSoftmaxWarps = NQ * kSoftmaxWarpsPerTile;
   static constexpr int kStats = kV + VST * kVStage;  // (max, sum) exchange, float2 per thread
   static constexpr int kBar = kStats + NQ * kThreadsPerRow * BM * 8;
-  static constexpr int kNumBars = 2 + 3 * KST + 3 * VST + 2 * NQ * kNSB + 3 * NQ + 2;
+  // fp32 P layout. kPAlias: P hi is written back into the score buffer it
+  // came from and every score buffer has a P-lo buffer of its own, so the
+  // softmax stores P_j while P@V_{j-1} still runs (one pv_done barrier per
+  // P-lo buffer); a score buffer is then reused after the P@V that read it.
+  // Otherwise one P hi and one P lo buffer, and a score buffer is reused
+  // once the softmax has read it. Measured: aliasing pays with 64-key tiles
+  // (head_dim 64) and costs with 32-key tiles (head_dim 128).
+  static constexpr bool kPAlias = kSplit && BN >= 64;
+  static constexpr int kPvBufs = kPAlias ? kNSB : 1;
+  static constexpr int kNumBars =
+      2 + 3 * KST + 3 * VST + 2 * NQ * kNSB + NQ * kPvBufs + 2 * NQ + 2;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 64 + 1024;  // + alignment slack
-  // TMEM columns per query tile: S buffers, O, and for fp32 one P hi and one
-  // P lo buffer plus the Q hi / Q lo operands of the score MMA. 16-bit P
+  // TMEM columns per query tile: S buffers, O, and for fp32 one P lo buffer
+  // per score buffer plus the Q hi / Q lo operands of the score MMA (fp32 P
+  // hi is written back into the score buffer it came from). 16-bit P
   // (packed pairs) goes back into the score buffer it came from: each
   // half-row thread packs its BN/2 keys into the first BN/4 columns of its
   // own half, so no thread overwrites scores another thread has yet to read.
-  static constexpr int kTileCols = kSplit ? kNSB * BN + 2 * BN + 3 * D : kNSB * BN + D;
+  static constexpr int kTileCols = !kSplit   ? kNSB * BN + D
+                                   : kPAlias ? 2 * kNSB * BN + 3 * D
+                                             : kNSB * BN + 2 * BN + 3 * D;
   static constexpr int kTCols = NQ * kTileCols;
   static constexpr uint32_t kTAlloc = kTCols <= 32    ? 32
                                       : kTCols <= 64  ? 64
@@ -224,12 +246,14 @@ struct TcLayout {
                                       : kTCols <= 256 ? 256
                                                       : 512;
   __host__ __device__ static constexpr int t_s(int t, int b) { return t * kTileCols + b * BN; }
-  __host__ __device__ static constexpr int t_phi(int t) { return t * kTileCols + kNSB * BN; }
-  __host__ __device__ static constexpr int t_plo(int t) {
-    return t * kTileCols + (kNSB + 1) * BN;
+  __host__ __device__ static constexpr int t_phi(int t, int b) {
+    return kPAlias ? t_s(t, b) : t * kTileCols + kNSB * BN;
+  }
+  __host__ __device__ static constexpr int t_plo(int t, int b) {
+    return t * kTileCols + (kNSB + (kPAlias ? b : 1)) * BN;
   }
   __host__ __device__ static constexpr int t_o(int t) {
-    return t * kTileCols + (kSplit ? (kNSB + 2) * BN : kNSB * BN);
+    return t * kTileCols + (!kSplit ? kNSB * BN : kPAlias ? 2 * kNSB * BN : (kNSB + 2) * BN);
   }
   __host__ __device__ static constexpr int t_qhi(int t) { return t_o(t) + D; }
   __host__ __device__ static constexpr int t_qlo(int t) { return t_o(t) + 2 * D; }
@@ -285,10 +309,12 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
   auto bar_s_full = [&](int t, int buf) { return tb + 8 * (t * NSB + buf); };
   auto bar_p_full = [&](int t, int buf) { return tb + 8 * (NQ * NSB + t * NSB + buf); };
   const uint32_t tb2 = tb + 8 * (2 * NQ * NSB);
-  auto bar_pv_done = [&](int t) { return tb2 + 8 * t; };
-  auto bar_stats = [&](int t) { return tb2 + 8 * (NQ + t); };
-  auto bar_o_empty = [&](int t) { return tb2 + 8 * (2 * NQ + t); };
-  const uint32_t bar_q_empty = tb2 + 8 * (3 * NQ);
+  constexpr int PVB = L::kPvBufs;
+  auto bar_pv_done = [&](int t, int b) { return tb2 + 8 * (t * PVB + b); };
+  const uint32_t tb3 = tb2 + 8 * (NQ * PVB);
+  auto bar_stats = [&](int t) { return tb3 + 8 * t; };
+  auto bar_o_empty = [&](int t) { return tb3 + 8 * (NQ + t); };
+  const uint32_t bar_q_empty = tb3 + 8 * (2 * NQ);
   const uint32_t bar_drain = bar_q_empty + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
@@ -315,7 +341,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         mbar_init(bar_s_full(t, bf), 1);
         mbar_init(bar_p_full(t, bf), 128 * L::kThreadsPerRow);
       }
-      mbar_init(bar_pv_done(t), 1);
+      for (int bf = 0; bf < PVB; ++bf) mbar_init(bar_pv_done(t, bf), 1);
       mbar_init(bar_stats(t), 128 * L::kThreadsPerRow);
       mbar_init(bar_o_empty(t), 128 * L::kThreadsPerRow);
     }
@@ -577,9 +603,10 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           constexpr int kPasses = kSplit ? 3 : 1;
 #pragma unroll
           for (int pass = 0; pass < kPasses; ++pass) {
-            const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, (kc + g) % NSB)
-                                    : pass == 0 ? tmem + L::t_plo(t)
-                                                : tmem + L::t_phi(t);
+            const int pb = (kc + g) % NSB;
+            const uint32_t p_tmem = !kSplit    ? tmem + L::t_s(t, pb)
+                                    : pass == 0 ? tmem + L::t_plo(t, pb)
+                                                : tmem + L::t_phi(t, pb);
             const int v_off = (kSplit && pass == 1) ? L::kKVBytes : 0;
 #pragma unroll
             for (int ks = 0; ks < kSteps; ++ks) {
@@ -601,7 +628,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
                 mma_ts_f16(o_tmem, a_tmem, bdesc, idesc_pv, acc);
             }
           }
-          tc_commit(bar_pv_done(t));
+          tc_commit(bar_pv_done(t, L::kPAlias ? (kc + g) % NSB : 0));
           if (t == NQ - 1) tc_commit(bar_v_empty(sv));
         }
         __syncwarp();
@@ -614,12 +641,17 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
 
       if constexpr (kSplit) {
         if (do_s) {
-          // a score buffer is reused once the softmax has read it; steps
-          // count across items, so every phase of every buffer is waited
-          // for in order (the first tiles of an item reuse the buffers of
-          // the previous item's last tiles)
+          // A score buffer is reused once the softmax has read it, or (P hi
+          // aliased into it) once the P@V that read P hi has completed.
+          // Steps count across items, so every phase of the awaited barrier
+          // is waited for in order (the first tiles of an item reuse the
+          // buffers of the previous item's last tiles).
           for (int g = 0; g < w.n_s && ok; ++g) {
-            if (kc + g >= NSB) ok = wait_p(0, g - NSB);
+            const int G = kc + g;
+            if (G >= NSB) {
+              ok = L::kPAlias ? wait_all(bar_pv_done(0, G % NSB), ((G - NSB) / NSB) & 1)
+                              : wait_p(0, g - NSB);
+            }
             if (ok) ok = issue_s(0, g);
           }
         } else {
@@ -900,7 +932,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             // Waiting for every P@V phase in order keeps the pv_done parity
             // barrier at most one phase ahead of this wait (and, with one
             // score buffer, PV_{j-1} has read P_{j-1} from these columns).
-            if (!__all_sync(0xFFFFFFFFu, wait(bar_pv_done(t), (vc + j - 1) & 1))) {
+            if (!__all_sync(0xFFFFFFFFu, wait(bar_pv_done(t, 0), (vc + j - 1) & 1))) {
               ok = false;
               break;
             }
@@ -918,7 +950,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         }
 
         // epilogue: this thread stores head_dim columns [half*D/2, (half+1)*D/2)
-        if (ok) ok = __all_sync(0xFFFFFFFFu, wait(bar_pv_done(t), (vc + w.n_kv - 1) & 1));
+        if (ok) ok = __all_sync(0xFFFFFFFFu, wait(bar_pv_done(t, 0), (vc + w.n_kv - 1) & 1));
         if (ok) {
           tc_fence_after();
           constexpr int DH = D / 2;
@@ -970,6 +1002,23 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       const float scale = p.scale;
       bool ok = true;
       int kc = 0, vc = 0, xc = 0;  // xc: completions of the exchange barrier so far
+      // P@V completions seen per pv_done barrier. Step G (counted across
+      // items) signals barrier G % PVB; the phases of each barrier are
+      // waited for in order and exactly once, so none can be skipped.
+      int pvs0 = 0, pvs1 = 0;
+      auto pv_seen_through = [&](int G) -> bool {  // P@V of every step <= G done
+#pragma unroll
+        for (int b = 0; b < PVB; ++b) {
+          if (G < b) continue;
+          const int last_use = (G - b) / PVB;
+          int& seen = b == 0 ? pvs0 : pvs1;
+          while (seen <= last_use) {
+            if (!__all_sync(0xFFFFFFFFu, wait(bar_pv_done(0, b), seen & 1))) return false;
+            ++seen;
+          }
+        }
+        return true;
+      };
       for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
         const Item w = item_at(it);
         const int row0 = w.q0;
@@ -1053,16 +1102,13 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           add2(part[4], part[5], part[6], part[7]);
           add2(part[0], part[1], part[4], part[5]);
           l_sum += part[0] + part[1];
-          // pv_done is a parity barrier: it only tells the current phase from
-          // the previous one. Waiting for every P@V phase in order (PV_{j-1}
-          // before storing P_j) keeps it at most one phase ahead, keeps P_{j-1}
-          // alive until its MMA has read it, and orders the O rescale after
-          // the MMA that wrote O.
-          if (j > 0) {
-            if (!__all_sync(0xFFFFFFFFu, wait(bar_pv_done(0), (vc + j - 1) & 1))) {
-              ok = false;
-              break;
-            }
+          // P_j's buffers were last read by PV_{j-PVB} (kPAlias: P hi into
+          // the score columns just read, P lo into P-lo buffer buf; else the
+          // single P hi / lo pair); an O rescale must also follow PV_{j-1},
+          // the last MMA that wrote O.
+          if (!pv_seen_through(sg - PVB) || (rescale && !pv_seen_through(sg - 1))) {
+            ok = false;
+            break;
           }
           if (rescale) {
             tc_fence_after();
@@ -1087,8 +1133,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
               ph[i] = hb;
               pl[i] = __float_as_uint(sv[i] - __uint_as_float(hb));
             }
-            tmem_st_cols<HB>(tmem + lane_off + L::t_phi(0) + c0, ph);
-            tmem_st_cols<HB>(tmem + lane_off + L::t_plo(0) + c0, pl);
+            tmem_st_cols<HB>(tmem + lane_off + L::t_phi(0, buf) + c0, ph);
+            tmem_st_cols<HB>(tmem + lane_off + L::t_plo(0, buf) + c0, pl);
           }
           tc_wait_st();
           tc_fence_before();
@@ -1108,7 +1154,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             l = half == 0 ? l_sum + other : other + l_sum;
           }
         }
-        if (ok) ok = __all_sync(0xFFFFFFFFu, wait(bar_pv_done(0), (vc + w.n_kv - 1) & 1));
+        if (ok) ok = pv_seen_through(vc + w.n_kv - 1);
         if (ok) {
           tc_fence_after();
           const float out_scale = l > 0.f ? 1.f / l : 0.f;
