@@ -258,3 +258,34 @@ def test_graph_switches_between_no_grad_and_inference_mode():
         c = graph(x)
     assert torch.equal(a, b) and torch.equal(b, c)
     assert graph.cuda_graph_replays == 3
+
+
+def _harness_close(a: torch.Tensor, b: torch.Tensor) -> bool:
+    err = (a.float() - b.float()).abs()
+    return bool(((err <= 1e-3) | (err <= 1e-2 * b.float().abs())).all())
+
+
+def test_forward_host_matches_the_device_forward_of_each_chunk():
+    torch.manual_seed(5)
+    model = UserOptimizedTransformer(TransformerConfig(8, 256, 256, 4, 1024, 2, True))
+    model = model.to("cuda").eval()
+    x_host = torch.randn(8, 256, 256).pin_memory()
+    lengths = torch.tensor([256, 200, 256, 17, 256, 256, 1, 128])
+    mask_host = torch.arange(256)[None, :] < lengths[:, None]
+    with torch.inference_mode():
+        y = model.forward_host(x_host, chunks=4)
+        assert y.device.type == "cpu" and y.is_pinned() and y.shape == x_host.shape
+        for i in range(4):
+            rows = slice(2 * i, 2 * i + 2)
+            assert torch.equal(y[rows], model(x_host[rows].cuda()).cpu())
+        assert _harness_close(y, model(x_host.cuda()).cpu())
+        ym = model.forward_host(x_host, mask_host, chunks=2)
+        for i in range(2):
+            rows = slice(4 * i, 4 * i + 4)
+            ref = model(x_host[rows].cuda(), mask_host[rows].cuda()).cpu()
+            assert torch.equal(ym[rows], ref)
+        out = torch.empty_like(x_host).pin_memory()
+        assert model.forward_host(x_host, out=out) is out
+        assert torch.equal(out, model.forward_host(x_host, chunks=model.default_host_chunks(8, 256)))
+        with pytest.raises(ValueError, match="divisor"):
+            model.forward_host(x_host, chunks=3)

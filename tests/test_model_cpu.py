@@ -105,3 +105,25 @@ def test_fused_route_reason_on_cpu():
     assert model.fused_route_reason(torch.randn(1, 8, 16), None) == "CPU input"
     sdpa = UserOptimizedTransformer(TransformerConfig(1, 8, 16, 2, 32, 1, False), "sdpa")
     assert "explicit math" in sdpa.fused_route_reason(torch.randn(1, 8, 16), None)
+
+
+def test_forward_host_on_a_cpu_model_is_forward():
+    cfg = TransformerConfig(4, 8, 16, 2, 32, 1, False)
+    model = UserOptimizedTransformer(cfg).eval()
+    x = torch.randn(4, 8, 16)
+    with torch.inference_mode():
+        ref = model(x)
+        assert torch.equal(model.forward_host(x, chunks=2), ref)
+        out = torch.empty_like(x)
+        assert model.forward_host(x, out=out) is out and torch.equal(out, ref)
+
+
+def test_default_host_chunks_keep_whole_sequences_and_enough_tokens():
+    chunks = UserOptimizedTransformer.default_host_chunks
+    assert chunks(8, 2048) == 2      # 4 sequences (8192 tokens) per chunk
+    assert chunks(512, 512) == 8     # capped at 8 chunks
+    assert chunks(4, 16384) == 4     # one sequence per chunk
+    assert chunks(4, 512) == 1       # too few tokens to split
+    assert chunks(7, 8192) == 7      # divisors of the batch only
+    assert chunks(7, 4096) == 1
+    assert chunks(1, 1) == 1

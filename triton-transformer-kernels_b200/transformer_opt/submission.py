@@ -57,6 +57,12 @@ EXECUTION_MODES = ("auto", "eager", "graph")
 # forwards keep the GPU busy without one, and replay would add an input copy
 # and an output copy.
 AUTO_GRAPH_MAX_ELEMENTS = 1 << 22
+# forward_host: default chunks keep at least this many tokens per chunk (the
+# GEMMs and the attention grid stay efficient; measured on C2 / C3 / C5) and
+# at most HOST_MAX_CHUNKS chunks.
+HOST_MIN_CHUNK_TOKENS = 8192
+HOST_MAX_CHUNKS = 8
+HOST_STREAMS = 3
 
 __all__ = ["TransformerConfig", "UserOptimizedTransformer"]
 
@@ -89,6 +95,7 @@ class UserOptimizedTransformer(TransformerWeights):
         self.fused_residual_layer_norm_calls = 0
         self.cuda_graph_replays = 0
         self._graph: Optional["_ForwardGraph"] = None
+        self._host_streams: Dict[int, Tuple[torch.cuda.Stream, ...]] = {}
         # Derived, non-persistent inference data keyed by id(attention module):
         # (parameter signature, packed weight [3d, d], packed bias [3d]).
         self._packed_qkv_cache: Dict[int, Tuple[tuple, torch.Tensor, torch.Tensor]] = {}
@@ -104,6 +111,7 @@ class UserOptimizedTransformer(TransformerWeights):
         state.pop("_lock", None)
         state["_packed_qkv_cache"] = {}
         state["_graph"] = None
+        state["_host_streams"] = {}
         return state
 
     def __setstate__(self, state):
@@ -221,6 +229,89 @@ class UserOptimizedTransformer(TransformerWeights):
             ):
                 return "LayerNorm parameters must be affine and in x's dtype"
         return None
+
+    # ------------------------------------------------------------ host batches
+    def forward_host(
+        self,
+        x: torch.Tensor,
+        valid_token_mask: Optional[torch.Tensor] = None,
+        *,
+        chunks: Optional[int] = None,
+        out: Optional[torch.Tensor] = None,
+    ) -> torch.Tensor:
+        """Forward of a batch held in host memory; returns the output in host memory.
+
+        The batch is split into ``chunks`` groups of whole sequences (a
+        divisor of the batch; by default the most groups, up to
+        HOST_MAX_CHUNKS, that keep HOST_MIN_CHUNK_TOKENS tokens each). Each
+        group's host-to-device copy, forward and device-to-host copy run in
+        order on one of HOST_STREAMS CUDA streams, so the transfers of one
+        group overlap the compute of the others. Sequences do not interact
+        in this model: the result is the forward of each group. Pinned host
+        memory makes the copies asynchronous (pageable memory works, with
+        synchronous copies). The call returns once ``out`` holds the result.
+        On a model outside CUDA this is ``forward``.
+        """
+        device = next(self.parameters()).device
+        if device.type != "cuda":
+            result = self.forward(x, valid_token_mask)
+            if out is not None:
+                out.copy_(result)
+                return out
+            return result
+        if x.dim() != 3:
+            raise ValueError(f"x must be [batch, seq, d_model], got {tuple(x.shape)}")
+        batch, seq = x.shape[0], x.shape[1]
+        if chunks is None:
+            chunks = self.default_host_chunks(batch, seq)
+        if chunks < 1 or batch % chunks != 0:
+            raise ValueError(
+                f"chunks must be a positive divisor of the batch ({batch}), got {chunks}"
+            )
+        if out is None:
+            out = torch.empty(x.shape, dtype=x.dtype, pin_memory=x.is_pinned())
+        elif out.shape != x.shape or out.dtype != x.dtype or out.device.type != "cpu":
+            raise ValueError("out must be a host tensor with x's shape and dtype")
+        streams = self._streams_for(device)
+        current = torch.cuda.current_stream(device)
+        step = batch // chunks
+        done = []
+        for i in range(chunks):
+            rows = slice(i * step, (i + 1) * step)
+            stream = streams[i % len(streams)]
+            stream.wait_stream(current)  # after the caller's earlier work
+            with torch.cuda.stream(stream):
+                xs = x[rows].to(device, non_blocking=True)
+                ms = None
+                if valid_token_mask is not None:
+                    ms = valid_token_mask[rows].to(device, non_blocking=True)
+                out[rows].copy_(self.forward(xs, ms), non_blocking=True)
+                event = torch.cuda.Event()
+                event.record(stream)
+                done.append(event)
+        for event in done:
+            current.wait_event(event)
+        for event in done:
+            event.synchronize()
+        return out
+
+    @staticmethod
+    def default_host_chunks(batch: int, seq: int) -> int:
+        """Chunk count ``forward_host`` uses when none is given."""
+        best = 1
+        for n in range(2, min(batch, HOST_MAX_CHUNKS) + 1):
+            if batch % n == 0 and (batch // n) * seq >= HOST_MIN_CHUNK_TOKENS:
+                best = n
+        return best
+
+    def _streams_for(self, device: torch.device) -> Tuple[torch.cuda.Stream, ...]:
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        with self._lock:
+            streams = self._host_streams.get(index)
+            if streams is None:
+                streams = tuple(torch.cuda.Stream(device=device) for _ in range(HOST_STREAMS))
+                self._host_streams[index] = streams
+            return streams
 
     def forward(
         self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
