@@ -821,8 +821,15 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             tc_fence_before();
             mbar_arrive(bar_p_full(t, buf));
           }
-          const bool masked =
-              HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
+          // A key-padding mask only forces the masked path where it drops a
+          // key of this half (the ballot words are warp-uniform: every lane
+          // of the warp covers the same keys).
+          bool pad = false;
+          if constexpr (HAS_MASK) {
+#pragma unroll
+            for (int wd = 0; wd < HB / 32; ++wd) pad = pad || kbits[wd] != 0xFFFFFFFFu;
+          }
+          const bool masked = pad || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
 
           // Scores with the reference's dtype boundaries, s = T(T(qk) * scale),
           // as fp32 pairs; masked keys become -inf. `mx` = max over the half.
@@ -1048,8 +1055,10 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
             tc_wait_ld();
 #pragma unroll
             for (int i = 0; i < HB; ++i) sv[i] = __uint_as_float(raw[i]) * scale;
-            const bool masked =
-                HAS_MASK || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
+            // lanes >= HB test keys beyond this half; only HB bits count
+            constexpr uint32_t kHalfBits = HB >= 32 ? 0xFFFFFFFFu : ((1u << HB) - 1u);
+            const bool pad = HAS_MASK && (kbits & kHalfBits) != kHalfBits;
+            const bool masked = pad || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
             if (masked) {
 #pragma unroll
               for (int i = 0; i < HB; ++i) {
