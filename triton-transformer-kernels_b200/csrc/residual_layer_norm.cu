@@ -21,6 +21,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <type_traits>
 
@@ -270,6 +271,53 @@ cudaError_t launch_vec(const RlnArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Resident CTAs per SM of one instantiation (occupancy query, made once; the
+// answer depends only on the kernel's resources and the SM architecture).
+template <typename T, int VPT, int TPR>
+int vec_ctas_per_sm() {
+  static std::atomic<int> cached{0};
+  int n = cached.load(std::memory_order_relaxed);
+  if (n == 0) {
+    constexpr int kBlock = TPR >= 256 ? TPR : 256;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rln_vec_kernel<T, VPT, TPR>, kBlock,
+                                                      0) != cudaSuccess ||
+        n < 1) {
+      (void)cudaGetLastError();
+      n = 1;
+    }
+    cached.store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+template <typename T, int TPR>
+int ctas_per_sm(int vpt) {
+  switch (vpt) {
+    case 1: return vec_ctas_per_sm<T, 1, TPR>();
+    case 2: return vec_ctas_per_sm<T, 2, TPR>();
+    case 3: return vec_ctas_per_sm<T, 3, TPR>();
+    case 4: return vec_ctas_per_sm<T, 4, TPR>();
+    case 5: return vec_ctas_per_sm<T, 5, TPR>();
+    case 6: return vec_ctas_per_sm<T, 6, TPR>();
+    case 7: return vec_ctas_per_sm<T, 7, TPR>();
+    default: return vec_ctas_per_sm<T, 8, TPR>();
+  }
+}
+
+// SM count of the current device, queried once per device.
+int current_sm_count() {
+  static std::atomic<int> counts[64] = {};
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 148;
+  int n = counts[device].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n < 1)
+      n = 148;
+    counts[device].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 template <typename T, int TPR>
 cudaError_t launch_vpt(const RlnArgs& a, int vpt, cudaStream_t stream) {
   switch (vpt) {
@@ -295,15 +343,43 @@ cudaError_t launch_typed(const RlnArgs& a, cudaStream_t stream) {
                        (aligned(a.update) && aligned(a.residual_out)));
   if (vec_ok) {
     const int64_t n_vec = a.width / EPV;
-    // smallest thread group per row that keeps <= 8 vectors per thread
-    const int tprs[3] = {32, 128, 512};
+    // Threads per row: the smallest group that keeps <= 8 vectors per thread,
+    // unless a wider group (never wider than the row's vectors) fills the
+    // last wave of CTAs clearly better. With few rows the number of waves is
+    // small and a mostly empty last wave dominates (fp32 d=4096, 2048 rows:
+    // 2.3 waves of 128-thread rows at 3 CTAs per SM).
+    const int tprs[4] = {32, 128, 256, 512};
+    const int sms = current_sm_count();
+    int best_tpr = 0, best_vpt = 0;
+    double best_fill = -1.0;
     for (int tpr : tprs) {
       const int64_t vpt = (n_vec + tpr - 1) / tpr;
-      if (vpt <= 8) {
-        if (tpr == 32) return launch_vpt<T, 32>(a, static_cast<int>(vpt), stream);
-        if (tpr == 128) return launch_vpt<T, 128>(a, static_cast<int>(vpt), stream);
-        return launch_vpt<T, 512>(a, static_cast<int>(vpt), stream);
+      if (vpt > 8) continue;
+      if (best_tpr != 0 && tpr > n_vec) break;
+      const int block = tpr >= 256 ? tpr : 256;
+      const int64_t grid = (a.rows + block / tpr - 1) / (block / tpr);
+      int per_sm = 1;
+      switch (tpr) {
+        case 32: per_sm = ctas_per_sm<T, 32>(static_cast<int>(vpt)); break;
+        case 128: per_sm = ctas_per_sm<T, 128>(static_cast<int>(vpt)); break;
+        case 256: per_sm = ctas_per_sm<T, 256>(static_cast<int>(vpt)); break;
+        default: per_sm = ctas_per_sm<T, 512>(static_cast<int>(vpt)); break;
       }
+      const double waves = static_cast<double>(grid) / (static_cast<double>(per_sm) * sms);
+      const double fill = waves / static_cast<double>(static_cast<int64_t>(waves) +
+                                                      (waves > static_cast<int64_t>(waves)));
+      if (best_tpr == 0 || fill > best_fill + 0.05) {
+        best_tpr = tpr;
+        best_vpt = static_cast<int>(vpt);
+        best_fill = fill;
+      }
+    }
+    switch (best_tpr) {
+      case 32: return launch_vpt<T, 32>(a, best_vpt, stream);
+      case 128: return launch_vpt<T, 128>(a, best_vpt, stream);
+      case 256: return launch_vpt<T, 256>(a, best_vpt, stream);
+      case 512: return launch_vpt<T, 512>(a, best_vpt, stream);
+      default: break;
     }
   }
   if (a.rows > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
