@@ -455,7 +455,9 @@ def run_b200_arm(args) -> int:
             # public host-buffer API: per chunk of sequences, H2D copy,
             # forward and D2H copy on their own stream (transfers overlap
             # compute); returns with the result in y_host
-            model.forward_host(x_host, out=y_host, chunks=e2e_chunks)
+            # the current stream waits for every chunk; the end event lands
+            # after the last D2H copy
+            model.forward_host(x_host, out=y_host, chunks=e2e_chunks, synchronize=False)
             e_ends[i].record(stream)
         torch.cuda.synchronize(device)
         y = y_host.to(device)  # the host-API result is the one validated

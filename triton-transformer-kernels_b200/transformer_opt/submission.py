@@ -238,6 +238,7 @@ class UserOptimizedTransformer(TransformerWeights):
         *,
         chunks: Optional[int] = None,
         out: Optional[torch.Tensor] = None,
+        synchronize: bool = True,
     ) -> torch.Tensor:
         """Forward of a batch held in host memory; returns the output in host memory.
 
@@ -249,8 +250,11 @@ class UserOptimizedTransformer(TransformerWeights):
         group overlap the compute of the others. Sequences do not interact
         in this model: the result is the forward of each group. Pinned host
         memory makes the copies asynchronous (pageable memory works, with
-        synchronous copies). The call returns once ``out`` holds the result.
-        On a model outside CUDA this is ``forward``.
+        synchronous copies). The call returns once ``out`` holds the result;
+        with ``synchronize=False`` it returns as soon as the work is queued,
+        the caller's current stream waits for all of it, and ``out`` may be
+        read after that stream is synchronised. A single chunk runs on the
+        caller's stream. On a model outside CUDA this is ``forward``.
         """
         device = next(self.parameters()).device
         if device.type != "cuda":
@@ -272,8 +276,15 @@ class UserOptimizedTransformer(TransformerWeights):
             out = torch.empty(x.shape, dtype=x.dtype, pin_memory=x.is_pinned())
         elif out.shape != x.shape or out.dtype != x.dtype or out.device.type != "cpu":
             raise ValueError("out must be a host tensor with x's shape and dtype")
-        streams = self._streams_for(device)
         current = torch.cuda.current_stream(device)
+        if chunks == 1:
+            xs = x.to(device, non_blocking=True)
+            ms = None if valid_token_mask is None else valid_token_mask.to(device, non_blocking=True)
+            out.copy_(self.forward(xs, ms), non_blocking=True)
+            if synchronize:
+                current.synchronize()
+            return out
+        streams = self._streams_for(device)
         step = batch // chunks
         done = []
         for i in range(chunks):
@@ -291,8 +302,9 @@ class UserOptimizedTransformer(TransformerWeights):
                 done.append(event)
         for event in done:
             current.wait_event(event)
-        for event in done:
-            event.synchronize()
+        if synchronize:
+            for event in done:
+                event.synchronize()
         return out
 
     @staticmethod
