@@ -128,6 +128,27 @@ def test_causal_frontier_at_tile_boundaries(seq, dim, mask_mode):
     assert_within_contract(out, ref)
 
 
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("dim,dtype", [(64, torch.float32), (128, torch.float32),
+                                       (64, torch.bfloat16), (128, torch.float16)])
+def test_padding_mask_only_changes_tiles_it_masks(dim, dtype, causal):
+    # An all-valid mask takes the same arithmetic as no mask (bitwise), and
+    # with a ragged mask the sequences whose keys are all valid match the
+    # unmasked result bitwise too.
+    torch.manual_seed(47)
+    q = torch.randn(3, 300, 2, dim, device="cuda", dtype=dtype)
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    plain = run_b200(q, k, v, causal=causal)
+    all_valid = torch.ones(3, 300, device="cuda", dtype=torch.bool)
+    assert torch.equal(run_b200(q, k, v, all_valid, causal=causal), plain)
+    ragged = torch.arange(300, device="cuda")[None, :] < torch.tensor([[300], [171], [300]], device="cuda")
+    out = run_b200(q, k, v, ragged, causal=causal)
+    assert torch.equal(out[0], plain[0]) and torch.equal(out[2], plain[2])
+    with torch.inference_mode():
+        ref = oracle.reference_attention(q[1:2], k[1:2], v[1:2], ragged[1:2], causal)
+    assert_within_contract(out[1:2], ref)
+
+
 @pytest.mark.parametrize("dim,dtype", [(32, torch.float32), (64, torch.float32), (128, torch.bfloat16)])
 def test_causal_future_tiles_are_never_observed(dim, dtype):
     torch.manual_seed(43)

@@ -177,17 +177,6 @@ __device__ __forceinline__ uint32_t max_pack2(uint32_t a, uint32_t b) {
   return d;
 }
 
-template <typename T>
-__device__ __forceinline__ uint32_t pack_pair(float a, float b) {
-  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  } else {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
-}
-
 template <typename T, int D, int BN, int KST, int VST, int NQ>
 struct TcLayout {
   static constexpr bool kSplit = ElemTraits<T>::kSplit;
