@@ -982,22 +982,28 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       }
     } else {
       // ------------------------------------------ softmax, fp32 (one pass)
-      // warp = 4*half + quad: key half `half` of every score tile, TMEM lane
-      // quadrant `quad`. The two threads of a row exchange their tile maxima
-      // through shared memory every tile (a bounded mbarrier round), so both
-      // keep the same running max, make the same rescale decision and each
-      // rescales its half of the O row.
-      constexpr int HB = BN / 2;
-      constexpr int DH = D / 2;
-      const int half = (warp >> 2) & 1;
+      // warp = 4 * blk + quad: rows 32 * quad + 16 * blk .. + 15 of the query
+      // tile (TMEM lane quadrant `quad`, 16-lane block `blk`). Scores, P and
+      // O are moved with the 16x256b shape: lane t holds rows t / 4 and
+      // t / 4 + 8 of the block and two columns of every 8-column group, so the
+      // four threads of a row are lanes 4i .. 4i + 3 of one warp and row
+      // maxima, rescale decisions and sums combine with shuffles (no shared
+      // memory round trip per tile).
+      constexpr int kRep = BN / 8;  // 16x256b repetitions per score tile
+      constexpr int NE = 4 * kRep;  // elements per thread: 2 rows x BN / 4 keys
       const int quad = warp & 3;
-      const int r = quad * 32 + lane;
-      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-      const int c0 = half * HB;
-      float* xchg = reinterpret_cast<float*>(smem + L::kStats);  // [2 slots][2 halves][BM]
+      const int blk = warp >> 2;
+      const int rb = quad * 32 + blk * 16;  // first row of this warp's block
+      const int ra = rb + (lane >> 2);      // this thread's rows: ra and ra + 8
+      const int cq = 2 * (lane & 3);        // its columns within each 8-column group
+      const uint32_t lane_off = static_cast<uint32_t>(rb) << 16;
+      // element e of a 16x256b fragment: row ra + 8 * ((e >> 1) & 1), column
+      // 8 * (e >> 2) + cq + (e & 1)
+      auto e_row = [&](int e) { return ra + 8 * ((e >> 1) & 1); };
+      auto e_col = [&](int e) { return 8 * (e >> 2) + cq + (e & 1); };
       const float scale = p.scale;
       bool ok = true;
-      int kc = 0, vc = 0, xc = 0;  // xc: completions of the exchange barrier so far
+      int kc = 0, vc = 0;
       // P@V completions seen per pv_done barrier. Step G (counted across
       // items) signals barrier G % PVB; the phases of each barrier are
       // waited for in order and exactly once, so none can be skipped.
@@ -1018,10 +1024,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
         const Item w = item_at(it);
         const int row0 = w.q0;
-        const int m = row0 + r;
-        const int warp_row0 = row0 + quad * 32;
-        float m_ref = -INFINITY;  // running max of the row, log2 units
-        float l_sum = 0.f;        // partial sum of this half
+        float m_ref[2] = {-INFINITY, -INFINITY};  // running row maxima, log2 units
+        float l_sum[2] = {0.f, 0.f};              // partial sums of this thread's columns
 
         for (int j = 0; j < w.n_s && ok; ++j) {
           const int sg = kc + j;
@@ -1029,77 +1033,89 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           ok = __all_sync(0xFFFFFFFFu, wait(bar_s_full(0, buf), (sg / NSB) & 1));
           if (!ok) break;
           tc_fence_after();
-          const int n0 = j * BN + c0;
-          float sv[HB];
+          const int n0 = j * BN;
+          float sv[NE];
           {
-            uint32_t raw[HB];
-            tmem_ld_cols<HB>(tmem + lane_off + L::t_s(0, buf) + c0, raw);
-            uint32_t kbits = 0xFFFFFFFFu;
+            uint32_t raw[NE];
+            tmem_ld16x256b<kRep>(tmem + lane_off + L::t_s(0, buf), raw);
+            // key-padding bits of the tile's keys (warp-uniform)
+            uint64_t kbits = ~0ull;
             if constexpr (HAS_MASK) {
-              const int n = n0 + lane;
-              bool valid = false;
-              if (n < p.seq) valid = p.mask[w.b * p.mask_sb + n * p.mask_ss] != 0;
-              kbits = __ballot_sync(0xFFFFFFFFu, valid);
+              kbits = 0;
+#pragma unroll
+              for (int wd = 0; wd < BN / 32; ++wd) {
+                const int n = n0 + wd * 32 + lane;
+                bool valid = false;
+                if (n < p.seq) valid = p.mask[w.b * p.mask_sb + n * p.mask_ss] != 0;
+                kbits |= static_cast<uint64_t>(__ballot_sync(0xFFFFFFFFu, valid)) << (32 * wd);
+              }
             }
             tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < HB; ++i) sv[i] = __uint_as_float(raw[i]) * scale;
-            // lanes >= HB test keys beyond this half; only HB bits count
-            constexpr uint32_t kHalfBits = HB >= 32 ? 0xFFFFFFFFu : ((1u << HB) - 1u);
-            const bool pad = HAS_MASK && (kbits & kHalfBits) != kHalfBits;
-            const bool masked = pad || (n0 + HB > p.seq) || (CAUSAL && n0 + HB - 1 > warp_row0);
+            for (int e = 0; e < NE; ++e) sv[e] = __uint_as_float(raw[e]) * scale;
+            constexpr uint64_t kTileBits = BN >= 64 ? ~0ull : ((1ull << BN) - 1ull);
+            const bool pad = HAS_MASK && (kbits & kTileBits) != kTileBits;
+            const bool masked =
+                pad || (n0 + BN > p.seq) || (CAUSAL && n0 + BN - 1 > row0 + rb);
             if (masked) {
 #pragma unroll
-              for (int i = 0; i < HB; ++i) {
-                const int n = n0 + i;
-                bool allowed = HAS_MASK ? ((kbits >> i) & 1u) != 0 : n < p.seq;
-                if (CAUSAL) allowed = allowed && (n <= m);
-                sv[i] = allowed ? sv[i] : -INFINITY;
+              for (int e = 0; e < NE; ++e) {
+                const int n = n0 + e_col(e);
+                bool allowed = HAS_MASK ? ((kbits >> e_col(e)) & 1ull) != 0 : n < p.seq;
+                if (CAUSAL) allowed = allowed && (n <= row0 + e_row(e));
+                sv[e] = allowed ? sv[e] : -INFINITY;
               }
             }
           }
-          // row max over both halves
-          float mx = row_max(sv);
-          const int slot = xc & 1;
-          xchg[(slot * 2 + half) * BM + r] = mx;
-          mbar_arrive(bar_stats(0));
-          ok = __all_sync(0xFFFFFFFFu, wait(bar_stats(0), xc & 1));
-          ++xc;
-          if (!ok) break;
-          mx = fmaxf(mx, xchg[(slot * 2 + (half ^ 1)) * BM + r]);
-
-          const float m_new = fmaxf(m_ref, mx * kLog2e);  // -inf stays -inf
-          bool rescale = false;
-          float alpha = 1.f;
-          if (j == 0) {
-            m_ref = m_new;
-          } else if (__any_sync(0xFFFFFFFFu, m_new > m_ref + kRescaleThreshold)) {
-            // the running max grew by more than 2^8: move every row of this
-            // warp to its new max (rows whose max did not grow keep alpha = 1).
-            // The partner warp sees the same maxima and decides the same way.
-            rescale = true;
-            if (m_new > m_ref) {
-              alpha = ex2_approx(m_ref - m_new);
-              m_ref = m_new;
-            }
-            l_sum *= alpha;
-          }
-          const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-          float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          // row maxima: this thread's columns, then the row's four threads
+          float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-          for (int i = 0; i < HB; i += 2) {
-            float a = sv[i], c = sv[i + 1];
-            fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
+          for (int e = 0; e < NE; ++e) mx[(e >> 1) & 1] = fmaxf(mx[(e >> 1) & 1], sv[e]);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 1));
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 2));
+          }
+          float m_new[2], alpha[2] = {1.f, 1.f};
+#pragma unroll
+          for (int h = 0; h < 2; ++h) m_new[h] = fmaxf(m_ref[h], mx[h] * kLog2e);  // -inf stays
+          bool rescale = false;
+          if (j == 0) {
+            m_ref[0] = m_new[0];
+            m_ref[1] = m_new[1];
+          } else if (__any_sync(0xFFFFFFFFu, m_new[0] > m_ref[0] + kRescaleThreshold ||
+                                                 m_new[1] > m_ref[1] + kRescaleThreshold)) {
+            // a running max grew by more than 2^8: move every row of this
+            // warp to its new max (rows whose max did not grow keep alpha = 1)
+            rescale = true;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (m_new[h] > m_ref[h]) {
+                alpha[h] = ex2_approx(m_ref[h] - m_new[h]);
+                m_ref[h] = m_new[h];
+              }
+              l_sum[h] *= alpha[h];
+            }
+          }
+          const float m_use[2] = {m_ref[0] == -INFINITY ? 0.f : m_ref[0],
+                                  m_ref[1] == -INFINITY ? 0.f : m_ref[1]};
+          float part[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+          for (int e = 0; e < NE; e += 2) {
+            const int h = (e >> 1) & 1;  // elements e, e + 1: same row
+            float a = sv[e], c = sv[e + 1];
+            fma2(a, c, kLog2e, kLog2e, -m_use[h], -m_use[h]);
             a = ex2_approx(a);
             c = ex2_approx(c);
-            sv[i] = a;
-            sv[i + 1] = c;
-            add2(part[i % 8], part[i % 8 + 1], a, c);
+            sv[e] = a;
+            sv[e + 1] = c;
+            add2(part[h][(e >> 2) & 1 ? 2 : 0], part[h][(e >> 2) & 1 ? 3 : 1], a, c);
           }
-          add2(part[0], part[1], part[2], part[3]);
-          add2(part[4], part[5], part[6], part[7]);
-          add2(part[0], part[1], part[4], part[5]);
-          l_sum += part[0] + part[1];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            add2(part[h][0], part[h][1], part[h][2], part[h][3]);
+            l_sum[h] += part[h][0] + part[h][1];
+          }
           // P_j's buffers were last read by PV_{j-PVB} (kPAlias: P hi into
           // the score columns just read, P lo into P-lo buffer buf; else the
           // single P hi / lo pair); an O rescale must also follow PV_{j-1},
@@ -1111,75 +1127,67 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
           if (rescale) {
             tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < DH / 32; ++c) {
+            for (int c = 0; c < D / 64; ++c) {
               uint32_t o[32];
-              const uint32_t addr = tmem + lane_off + L::t_o(0) + half * DH + c * 32;
-              tmem_ld32(addr, o);
+              const uint32_t addr = tmem + lane_off + L::t_o(0) + c * 64;
+              tmem_ld16x256b<8>(addr, o);
               tc_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(addr, o);
+              for (int e = 0; e < 32; ++e)
+                o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha[(e >> 1) & 1]);
+              tmem_st16x256b<8>(addr, o);
             }
           }
           {
             // P hi keeps the tf32 bits, P lo the exact remainder
-            uint32_t ph[HB], pl[HB];
+            uint32_t ph[NE], pl[NE];
 #pragma unroll
-            for (int i = 0; i < HB; ++i) {
-              const uint32_t hb = __float_as_uint(sv[i]) & 0xFFFFE000u;
-              ph[i] = hb;
-              pl[i] = __float_as_uint(sv[i] - __uint_as_float(hb));
+            for (int e = 0; e < NE; ++e) {
+              const uint32_t hb = __float_as_uint(sv[e]) & 0xFFFFE000u;
+              ph[e] = hb;
+              pl[e] = __float_as_uint(sv[e] - __uint_as_float(hb));
             }
-            tmem_st_cols<HB>(tmem + lane_off + L::t_phi(0, buf) + c0, ph);
-            tmem_st_cols<HB>(tmem + lane_off + L::t_plo(0, buf) + c0, pl);
+            tmem_st16x256b<kRep>(tmem + lane_off + L::t_phi(0, buf), ph);
+            tmem_st16x256b<kRep>(tmem + lane_off + L::t_plo(0, buf), pl);
           }
           tc_wait_st();
           tc_fence_before();
           mbar_arrive(bar_p_full(0, buf));
         }
 
-        // epilogue: combine the two partial row sums, store this half of O
-        float l = 0.f;
-        if (ok) {
-          const int slot = xc & 1;
-          xchg[(slot * 2 + half) * BM + r] = l_sum;
-          mbar_arrive(bar_stats(0));
-          ok = __all_sync(0xFFFFFFFFu, wait(bar_stats(0), xc & 1));
-          ++xc;
-          if (ok) {
-            const float other = xchg[(slot * 2 + (half ^ 1)) * BM + r];
-            l = half == 0 ? l_sum + other : other + l_sum;
-          }
+        // epilogue: row sums over the row's four threads (every thread adds
+        // the same pairs: the result is bitwise the same on all four), then
+        // this thread's columns of O for its two rows
+        float out_scale[2] = {0.f, 0.f};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float l = l_sum[h] + __shfl_xor_sync(0xFFFFFFFFu, l_sum[h], 1);
+          l = l + __shfl_xor_sync(0xFFFFFFFFu, l, 2);
+          out_scale[h] = l > 0.f ? 1.f / l : 0.f;
         }
         if (ok) ok = pv_seen_through(vc + w.n_kv - 1);
         if (ok) {
           tc_fence_after();
-          const float out_scale = l > 0.f ? 1.f / l : 0.f;
-          float* out_row = reinterpret_cast<float*>(p.out) +
-                           ((static_cast<int64_t>(w.b) * p.seq + m) * p.heads + w.h) * D +
-                           half * DH;
-          const bool row_ok = m < p.seq;
 #pragma unroll 1
-          for (int c = 0; c < DH / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             uint32_t o[32];
-            tmem_ld32(tmem + lane_off + L::t_o(0) + half * DH + c * 32, o);
+            tmem_ld16x256b<8>(tmem + lane_off + L::t_o(0) + c * 64, o);
             tc_wait_ld();
-            if (c == DH / 32 - 1) {
+            if (c == D / 64 - 1) {
               // O has been read: the next item's first P@V may overwrite it
               tc_fence_before();
               mbar_arrive(bar_o_empty(0));
             }
-            if (row_ok) {
-              float4* dst = reinterpret_cast<float4*>(out_row + c * 32);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                float4 v;
-                v.x = __uint_as_float(o[4 * i + 0]) * out_scale;
-                v.y = __uint_as_float(o[4 * i + 1]) * out_scale;
-                v.z = __uint_as_float(o[4 * i + 2]) * out_scale;
-                v.w = __uint_as_float(o[4 * i + 3]) * out_scale;
-                dst[i] = v;
+            for (int e = 0; e < 32; e += 2) {
+              const int m = row0 + e_row(e);
+              if (m < p.seq) {
+                float* dst = reinterpret_cast<float*>(p.out) +
+                             ((static_cast<int64_t>(w.b) * p.seq + m) * p.heads + w.h) * D +
+                             c * 64 + e_col(e);
+                const float sc = out_scale[(e >> 1) & 1];
+                *reinterpret_cast<float2*>(dst) =
+                    make_float2(__uint_as_float(o[e]) * sc, __uint_as_float(o[e + 1]) * sc);
               }
             }
           }
