@@ -29,6 +29,7 @@ cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
   prm.n_qtiles = 0;  // set per tile configuration
   prm.scale = a.scale;
   prm.causal_reverse = 1;
+  prm.causal_pairs = 1;
   // T(T(qk) * 2^k) == T(qk) * 2^k for bf16 (fp32 exponent range), so the
   // kernel may skip the second rounding; not for fp16 (subnormals round).
   int exponent = 0;

@@ -68,6 +68,7 @@ struct __align__(64) AttnTcParams {
   int batch, seq, heads, n_qtiles;
   float scale;
   int causal_reverse;  // schedule longest causal tiles first
+  int causal_pairs;    // persistent causal schedule over (long, short) tile pairs
   int scale_pow2;      // bf16 only: scale is an exact power of two
   unsigned int* status;
 };
@@ -361,15 +362,54 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
   // reference's rounding boundary (softmax in fp32, then cast, then P@V).
   // fp32 inputs take one online pass (P keeps ~fp32 precision through the
   // 3xTF32 split, so normalising at the end is equivalent).
-  const int total_items = p.n_qtiles * p.batch * p.heads;
+  //
+  // Causal items get longer with the query tile. With causal_pairs the
+  // launch is persistent too: item index 2 * pair + member, where pair
+  // (bh, pos) holds query tiles n - 1 - pos (member 0) and pos (member 1),
+  // whose costs add up to the same for every pair; CTA c takes pairs c,
+  // c + grid, ... (pairs of one batch-head are adjacent, so the CTAs in
+  // flight share a few heads' K/V in L2). With an odd tile count the middle
+  // tile's pair has one member.
+  const int pair_half = (p.n_qtiles + 1) / 2;  // pairs per batch-head
+  const int total_items = (CAUSAL && p.causal_pairs)
+                              ? 2 * pair_half * p.batch * p.heads
+                              : p.n_qtiles * p.batch * p.heads;
+  auto item_valid = [&](int it) {
+    if (!(CAUSAL && p.causal_pairs) || !(it & 1)) return true;
+    const int pos = (it >> 1) % pair_half;
+    return pos != p.n_qtiles - 1 - pos;
+  };
+  // first item of this CTA / the one after `it` (same sequence in every role)
+  auto first_item = [&]() {
+    int it = (CAUSAL && p.causal_pairs) ? 2 * static_cast<int>(blockIdx.x)
+                                        : static_cast<int>(blockIdx.x);
+    return it;
+  };
+  auto next_item = [&](int it) {
+    if (CAUSAL && p.causal_pairs) {
+      do {
+        it = (it & 1) ? it + 2 * static_cast<int>(gridDim.x) - 1 : it + 1;
+      } while (it < total_items && !item_valid(it));
+      return it;
+    }
+    return it + static_cast<int>(gridDim.x);
+  };
   struct Item {
     int b, h, q0, n_kv, n_s;
   };
   auto item_at = [&](int it) {
     Item w;
-    const int bh = it / p.n_qtiles;
-    int qt = it - bh * p.n_qtiles;
-    if (CAUSAL && p.causal_reverse) qt = p.n_qtiles - 1 - qt;
+    int bh, qt;
+    if (CAUSAL && p.causal_pairs) {
+      const int pair = it >> 1;
+      bh = pair / pair_half;
+      const int pos = pair - bh * pair_half;
+      qt = (it & 1) ? pos : p.n_qtiles - 1 - pos;
+    } else {
+      bh = it / p.n_qtiles;
+      qt = it - bh * p.n_qtiles;
+      if (CAUSAL && p.causal_reverse) qt = p.n_qtiles - 1 - qt;
+    }
     w.b = bh / p.heads;
     w.h = bh - w.b * p.heads;
     w.q0 = qt * NQ * BM;
@@ -393,7 +433,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       int issued_v[VST] = {};
       bool ok = true;
       int kc = 0, vc = 0, items_loaded = 0;
-      for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+      for (int it = first_item(), k = 0; it < total_items && ok; it = next_item(it), ++k) {
         const Item w = item_at(it);
         auto tile_of = [&](int g) { return (kTwoPass && g >= w.n_kv) ? g - w.n_kv : g; };
         // Q smem (and, for fp32, the Q operand in TMEM) is free once every
@@ -514,7 +554,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
     };
     bool ok = true;
     int kc = 0, vc = 0;
-    for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+    for (int it = first_item(), k = 0; it < total_items && ok; it = next_item(it), ++k) {
       const Item w = item_at(it);
       auto tile_of = [&](int g) { return (kTwoPass && g >= w.n_kv) ? g - w.n_kv : g; };
       if (do_s) {
@@ -693,7 +733,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
     };
     bool ok = true;
     int kc = 0, vc = 0;
-    for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+    for (int it = first_item(), k = 0; it < total_items && ok; it = next_item(it), ++k) {
       const Item w = item_at(it);
       ok = wait(bar_q_full, k & 1);
       // the previous item's score MMAs read the Q operand in TMEM
@@ -770,7 +810,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
       const bool pow2 = p.scale_pow2 != 0;
       bool ok = true;
       int kc = 0, vc = 0;
-      for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+      for (int it = first_item(), k = 0; it < total_items && ok; it = next_item(it), ++k) {
         const Item w = item_at(it);
         const int row0 = w.q0 + t * BM;
         const int m = row0 + r;
@@ -1021,7 +1061,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         }
         return true;
       };
-      for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
+      for (int it = first_item(), k = 0; it < total_items && ok; it = next_item(it), ++k) {
         const Item w = item_at(it);
         const int row0 = w.q0;
         float m_ref[2] = {-INFINITY, -INFINITY};  // running row maxima, log2 units
@@ -1260,10 +1300,14 @@ cudaError_t launch_dtype_hd(AttnTcParams prm, int num_sms, bool causal, bool has
   // Non-causal items all cost the same: one persistent CTA per SM loops over
   // them (barriers and TMEM set up once, the next item's loads overlap the
   // current item's tail). Causal items differ in length by up to the number
-  // of query tiles; a CTA per item lets the hardware block scheduler balance
-  // them (longest first), which a static round-robin assignment cannot.
-  const int grid =
-      static_cast<int>(causal ? items : (items < num_sms ? items : static_cast<int64_t>(num_sms)));
+  // of query tiles: with causal_pairs the persistent CTAs take equal-cost
+  // (long, short) pairs of tiles, otherwise a CTA per item lets the hardware
+  // block scheduler balance them (longest first).
+  int64_t work = items;  // schedulable units: items, or pairs of items
+  if (causal && prm.causal_pairs)
+    work = static_cast<int64_t>((prm.n_qtiles + 1) / 2) * prm.batch * prm.heads;
+  const bool persistent = !causal || prm.causal_pairs;
+  const int grid = static_cast<int>(persistent ? (work < num_sms ? work : num_sms) : work);
   if (causal)
     return has_mask
                ? launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, true, true>(prm, grid, stream)
