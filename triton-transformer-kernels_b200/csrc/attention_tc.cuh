@@ -28,7 +28,8 @@
 //                     so each product runs as lo*hi + hi*lo + hi*hi.
 // Causal key tiles beyond the item's last query row are never loaded (the key
 // loop ends at min(S, last row + 1)), the reference's end bound (:163-166).
-// Non-causal launches are persistent (one CTA per SM walking the items).
+// Launches are persistent (at most one CTA per SM walking the items; causal
+// items are taken in (long, short) query-tile pairs of equal cost).
 //
 // Every mbarrier wait is bounded (ptx_sm100.cuh mbar_wait): on timeout the
 // CTA raises an abort flag and a device status bit, drains its own copies and
