@@ -149,6 +149,19 @@ def test_padding_mask_only_changes_tiles_it_masks(dim, dtype, causal):
     assert_within_contract(out[1:2], ref)
 
 
+@pytest.mark.parametrize("scale", [0.3, -0.125])
+@pytest.mark.parametrize("dim,dtype", [(64, torch.float32), (128, torch.float32), (64, torch.bfloat16)])
+def test_custom_and_negative_scales(dim, dtype, scale):
+    torch.manual_seed(53)
+    q = torch.randn(2, 200, 2, dim, device="cuda", dtype=dtype)
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    for causal in (False, True):
+        out = run_b200(q, k, v, causal=causal, scale=scale)
+        with torch.inference_mode():
+            ref = oracle.reference_attention(q, k, v, None, causal, scale=scale)
+        assert_within_contract(out, ref)
+
+
 @pytest.mark.parametrize("dim,dtype", [(32, torch.float32), (64, torch.float32), (128, torch.bfloat16)])
 def test_causal_future_tiles_are_never_observed(dim, dtype):
     torch.manual_seed(43)
