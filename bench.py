@@ -52,11 +52,11 @@ L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 # DRAM bytes per attention launch (dram__bytes_read.sum + dram__bytes_write.sum)
 # from one ncu capture of the same kernel and workload; see profiles/.
 NCU_ATTENTION_TRAFFIC = {
-    # profiles/attention_fwd_tc_fp32_C2.md: 201.5 MB read + 49.5 MB written
-    "C2": 251.0e6,
-    # profiles/attention_fwd_tc_bf16_C3.md: captured at batch 1 (406.3 MB read
-    # + 121.6 MB written), scaled by C3's 4 independent sequences
-    "C3": 4 * 527.9e6,
+    # profiles/attention_fwd_tc_fp32_C2.md: 201.5 MB read + 48.3 MB written
+    "C2": 249.8e6,
+    # profiles/attention_fwd_tc_bf16_C3.md: captured at batch 1 (424.0 MB read
+    # + 113.8 MB written), scaled by C3's 4 independent sequences
+    "C3": 4 * 537.7e6,
 }
 
 
