@@ -289,6 +289,15 @@ def test_forward_host_matches_the_device_forward_of_each_chunk():
         assert torch.equal(out, model.forward_host(x_host, chunks=model.default_host_chunks(8, 256)))
         with pytest.raises(ValueError, match="divisor"):
             model.forward_host(x_host, chunks=3)
+        # explicit (unequal) chunk sizes: each group is its own device forward
+        ys = model.forward_host(x_host, chunks=[1, 3, 2, 2])
+        start = 0
+        for size in (1, 3, 2, 2):
+            rows = slice(start, start + size)
+            start += size
+            assert torch.equal(ys[rows], model(x_host[rows].cuda()).cpu())
+        with pytest.raises(ValueError, match="sum to the batch"):
+            model.forward_host(x_host, chunks=[4, 3])
 
 
 def test_forward_host_without_synchronize_is_ordered_on_the_current_stream():

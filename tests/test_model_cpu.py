@@ -120,10 +120,24 @@ def test_forward_host_on_a_cpu_model_is_forward():
 
 def test_default_host_chunks_keep_whole_sequences_and_enough_tokens():
     chunks = UserOptimizedTransformer.default_host_chunks
-    assert chunks(8, 2048) == 2      # 4 sequences (8192 tokens) per chunk
+    assert chunks(8, 2048) == 4      # 2 sequences (4096 tokens) per chunk
     assert chunks(512, 512) == 8     # capped at 8 chunks
     assert chunks(4, 16384) == 4     # one sequence per chunk
     assert chunks(4, 512) == 1       # too few tokens to split
-    assert chunks(7, 8192) == 7      # divisors of the batch only
-    assert chunks(7, 4096) == 1
+    assert chunks(7, 4096) == 7      # divisors of the batch only
+    assert chunks(7, 2048) == 1
     assert chunks(1, 1) == 1
+    plan = UserOptimizedTransformer.default_host_plan
+    assert plan(8, 2048) == [2, 2, 2, 2]                  # halves would hold 2048 tokens
+    assert plan(512, 512) == [32] + [64] * 7 + [32]       # first and last chunks halved
+    assert plan(4, 16384) == [1, 1, 1, 1]
+    assert sum(plan(512, 512)) == 512
+
+
+def test_forward_host_accepts_chunk_sizes_on_a_cpu_model():
+    cfg = TransformerConfig(4, 8, 16, 2, 32, 1, False)
+    model = UserOptimizedTransformer(cfg).to("cpu").eval()
+    x = torch.randn(4, 8, 16)
+    with torch.inference_mode():
+        ref = model(x)
+        assert torch.equal(model.forward_host(x, chunks=[1, 3]), ref)  # CPU: plain forward
