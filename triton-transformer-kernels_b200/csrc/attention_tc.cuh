@@ -206,8 +206,10 @@ struct TcLayout {
   static constexpr int kThreadsPerRow = 2;
   static constexpr int kSoftmaxWarpsPerTile = 4 * kThreadsPerRow;
   static constexpr int kSoftmaxWarps = NQ * kSoftmaxWarpsPerTile;
-  static constexpr int kStats = kV + VST * kVStage;  // (max, sum) exchange, float2 per thread
-  static constexpr int kBar = kStats + NQ * kThreadsPerRow * BM * 8;
+  // 16-bit (max, sum) exchange at the end of pass 1, float2 per thread (fp32
+  // combines its row statistics with shuffles and needs none)
+  static constexpr int kStats = kV + VST * kVStage;
+  static constexpr int kBar = kStats + (kSplit ? 0 : NQ * kThreadsPerRow * BM * 8);
   // fp32 P layout. kPAlias: P hi is written back into the score buffer it
   // came from and every score buffer has a P-lo buffer of its own, so the
   // softmax stores P_j while P@V_{j-1} still runs (one pv_done barrier per
@@ -221,9 +223,10 @@ struct TcLayout {
       2 + 3 * KST + 3 * VST + 2 * NQ * kNSB + NQ * kPvBufs + 2 * NQ + 2;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 64 + 1024;  // + alignment slack
-  // TMEM columns per query tile: S buffers, O, and for fp32 one P lo buffer
-  // per score buffer plus the Q hi / Q lo operands of the score MMA (fp32 P
-  // hi is written back into the score buffer it came from). 16-bit P
+  // TMEM columns per query tile: S buffers, O, and for fp32 the P buffers
+  // (kPAlias: a P lo buffer per score buffer, P hi written back into the
+  // score buffer it came from; else one P hi and one P lo buffer) plus the
+  // Q hi / Q lo operands of the score MMA. 16-bit P
   // (packed pairs) goes back into the score buffer it came from: each
   // half-row thread packs its BN/2 keys into the first BN/4 columns of its
   // own half, so no thread overwrites scores another thread has yet to read.
