@@ -1,7 +1,7 @@
 /*
  * b200tk.h - C ABI of libb200tk.so, the sm_100a (B200) kernels behind the
- * Transformer inference hot path: fused attention forward and fused
- * residual-add + LayerNorm.
+ * Transformer inference hot path: fused attention forward, fused
+ * residual-add + LayerNorm, and the FFN input projection with its GELU.
  *
  * Every entry point takes plain device pointers, element strides, sizes and a
  * cudaStream_t passed as void*. Nothing here allocates device memory, blocks
@@ -14,9 +14,11 @@
  * Device-side pipeline timeouts are not return codes: they are recorded in a
  * per-device status word that b200tk_device_status() reads.
  *
- * The reference implements these two operations as Triton kernels behind
- * Python wrappers; it has no C ABI. The citations below name the reference
- * function each entry point replaces (paths inside the reference project).
+ * The reference implements attention and residual + LayerNorm as Triton
+ * kernels behind Python wrappers, and the FFN projection as a cuBLAS GEMM
+ * followed by an elementwise GELU; it has no C ABI. The citations below name
+ * the reference code each entry point replaces (paths inside the reference
+ * project).
  */
 #ifndef B200TK_H
 #define B200TK_H
@@ -122,6 +124,29 @@ B200TK_API int b200tk_residual_layer_norm_fwd(const void* x, const void* update,
                                    void* residual_out, void* normalized_out, int dtype,
                                    int64_t rows, int64_t width, float eps, uint32_t flags,
                                    void* stream);
+
+/*
+ * FFN input projection with its activation fused into the GEMM epilogue:
+ *   out[m, n] = gelu(sum_k x[m, k] * weight[n, k] + bias[n])
+ * with the exact (erf) GELU, v * 0.5 * (1 + erf(v / sqrt(2))).
+ *
+ * Replaces: the `F.gelu(layer.ffn_in(h), approximate="none")` pair of the
+ * reference's block (benchmarks/torch_transformer_benchmark.py:131, 141), as
+ * placed by its fused layer loop at transformer_opt/submission.py:506-508
+ * (there: a cuBLAS GEMM followed by a separate elementwise GELU pass).
+ *
+ * x      : [rows, in_features] row-major.   weight : [out_features, in_features]
+ *          row-major (nn.Linear layout).     bias : [out_features] or NULL.
+ * out    : [rows, out_features] row-major, in `dtype`.
+ * Accumulation and bias are fp32. float32 multiplies as TF32 (the precision of
+ * an fp32 matmul with TF32 allowed); float16/bfloat16 round the biased sum to
+ * dtype before the GELU, as the unfused Linear's output tensor does.
+ * in_features and out_features must be multiples of 16 bytes of elements and
+ * every pointer 16-byte aligned (B200TK_ERR_UNSUPPORTED otherwise).
+ */
+B200TK_API int b200tk_linear_gelu_fwd(const void* x, const void* weight, const void* bias,
+                                      void* out, int dtype, int64_t rows, int64_t in_features,
+                                      int64_t out_features, void* stream);
 
 /*
  * Read (and, with clear != 0, reset) the device status word of `device`.

@@ -16,7 +16,9 @@ explicit model and per-op semantics:
               abs_err <= atol OR abs_err <= rtol * |ref|, not isclose).
   * per-op  : reference_attention = transformer_opt/dispatch.py:69-96;
               residual_layer_norm = tests/test_gpu_residual_layer_norm.py:44-61
-              (x + update, optional invalid-row zeroing, F.layer_norm).
+              (x + update, optional invalid-row zeroing, F.layer_norm);
+              linear_gelu = the block's FFN input projection + exact GELU,
+              benchmarks/torch_transformer_benchmark.py:141.
 Parity is pinned by tests/test_oracle_golden.py against golden vectors that
 tests/golden/make_golden.py produced by running the reference itself.
 """
@@ -277,6 +279,16 @@ def residual_layer_norm(
     if zero_invalid_normalized:
         normalized = normalized.masked_fill(~valid_token_mask[..., None], 0)
     return residual, normalized
+
+
+def linear_gelu(
+    x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]
+) -> torch.Tensor:
+    """The block's FFN input projection and activation,
+    ``F.gelu(ffn_in(h), approximate="none")``
+    (benchmarks/torch_transformer_benchmark.py:141): a Linear whose output is
+    a tensor of x's dtype, then the exact (erf) GELU of that tensor."""
+    return F.gelu(F.linear(x, weight, bias), approximate="none")
 
 
 

@@ -1,5 +1,6 @@
 // attention.h - internal launch interfaces shared by the C ABI (capi.cu) and
-// the attention kernels. Not part of the public ABI.
+// the kernels (attention, residual + LayerNorm, linear + GELU). Not part of
+// the public ABI.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -62,6 +63,19 @@ struct RlnArgs {
   uint32_t flags;
 };
 cudaError_t launch_residual_layer_norm(const RlnArgs& args, cudaStream_t stream);
+
+// Linear + exact GELU (the FFN input projection). Tensor maps are built by
+// the host: x [rows, k_in] and weight [n_out, k_in], both row-major.
+struct LinearGeluArgs {
+  alignas(64) unsigned char tm_x[128];
+  alignas(64) unsigned char tm_w[128];
+  const void* bias;
+  void* out;
+  int64_t rows, k_in, n_out;
+  int dtype;
+  unsigned int* status;
+};
+cudaError_t launch_linear_gelu(const LinearGeluArgs& args, cudaStream_t stream);
 
 // Failure-detection self test (bounded wait on an mbarrier nobody completes).
 cudaError_t launch_selftest_wait_timeout(unsigned int* status, uint32_t timeout_us,

@@ -29,6 +29,7 @@ UNITS = [
     ("attention_tc.cu", "attention_tc", ()),
     ("attention_generic.cu", "attention_generic", ()),
     ("residual_layer_norm.cu", "residual_layer_norm", ()),
+    ("linear_gelu.cu", "linear_gelu", ()),
 ] + [
     (
         "attention_tc_inst.cu",

@@ -125,6 +125,33 @@ int encode_map(void* out, const void* ptr, const int64_t* st, int64_t batch, int
   return B200TK_OK;
 }
 
+// Row-major [rows, cols] matrix as a 2D tensor map: box {128 bytes of
+// columns, box_rows rows}, 128-byte swizzle. Out-of-range rows and columns
+// read as zero.
+int encode_matrix_map(void* out, const void* ptr, int64_t rows, int64_t cols, int dtype,
+                      int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  int rc = get_encoder(&enc);
+  if (rc != B200TK_OK) return rc;
+  const int es = elem_size(dtype);
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * es)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapDataType dt = dtype == B200TK_DTYPE_FLOAT32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : dtype == B200TK_DTYPE_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = enc(reinterpret_cast<CUtensorMap*>(out), dt, 2, const_cast<void*>(ptr), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+    return fail(B200TK_ERR_CUDA, buf);
+  }
+  return B200TK_OK;
+}
+
 int validate_attention(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
                        const void* v, const int64_t* vs, int dtype, int64_t batch, int64_t seq,
                        int64_t heads, int64_t head_dim) {
@@ -303,6 +330,43 @@ int b200tk_residual_layer_norm_fwd(const void* x, const void* update, const void
   a.flags = flags;
   cudaError_t err = launch_residual_layer_norm(a, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "residual layer norm launch");
+  return B200TK_OK;
+}
+
+int b200tk_linear_gelu_fwd(const void* x, const void* weight, const void* bias, void* out,
+                           int dtype, int64_t rows, int64_t in_features, int64_t out_features,
+                           void* stream) {
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(B200TK_ERR_INVALID_ARGUMENT, "unknown dtype code");
+  if (rows < 0 || in_features <= 0 || out_features <= 0)
+    return fail(B200TK_ERR_INVALID_ARGUMENT, "rows >= 0, in_features > 0 and out_features > 0");
+  if (rows > (int64_t(1) << 31) - 256 || out_features > (int64_t(1) << 30) ||
+      in_features > (int64_t(1) << 30))
+    return fail(B200TK_ERR_UNSUPPORTED, "matrix extent exceeds the kernel's index range");
+  if ((in_features * es) % 16 != 0 || (out_features * es) % 16 != 0)
+    return fail(B200TK_ERR_UNSUPPORTED,
+                "in_features and out_features must be multiples of 16 bytes of elements");
+  if (rows == 0) return B200TK_OK;
+  if (x == nullptr || weight == nullptr || out == nullptr)
+    return fail(B200TK_ERR_INVALID_ARGUMENT, "x, weight and out must not be NULL");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(out) ||
+      (bias != nullptr && !aligned16(bias)))
+    return fail(B200TK_ERR_UNSUPPORTED, "x, weight, bias and out must be 16-byte aligned");
+  LinearGeluArgs a;
+  std::memset(&a, 0, sizeof(a));
+  int rc = encode_matrix_map(a.tm_x, x, rows, in_features, dtype, 128);
+  if (rc == B200TK_OK) rc = encode_matrix_map(a.tm_w, weight, out_features, in_features, dtype, 128);
+  if (rc != B200TK_OK) return rc;
+  rc = status_address(&a.status);
+  if (rc != B200TK_OK) return rc;
+  a.bias = bias;
+  a.out = out;
+  a.rows = rows;
+  a.k_in = in_features;
+  a.n_out = out_features;
+  a.dtype = dtype;
+  cudaError_t err = launch_linear_gelu(a, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "linear gelu launch");
   return B200TK_OK;
 }
 

@@ -53,6 +53,7 @@ SIGNATURES = {
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, ctypes.c_float, ctypes.c_uint32, _P],
     ),
+    "b200tk_linear_gelu_fwd": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
     "b200tk_device_status": (_I, [_I, ctypes.POINTER(ctypes.c_uint32), _I]),
     "b200tk_selftest_wait_timeout": (_I, [_I, ctypes.c_uint32, _P]),
 }
@@ -194,6 +195,23 @@ def residual_layer_norm_fwd(
         ptr(x), ptr(update), ptr(weight), ptr(bias), ptr(mask),
         ptr(residual_out), ptr(normalized_out),
         DTYPE_CODES[x.dtype], rows, width, float(eps), int(flags),
+        _stream_handle(x.device),
+    )
+    _check(rc)
+
+
+def linear_gelu_fwd(
+    x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], out: torch.Tensor
+) -> None:
+    """Launch out = gelu(x @ weight.T + bias) on the current stream of x's device."""
+    lib = load()
+    in_features = x.shape[-1]
+    rows = x.numel() // in_features if in_features else 0
+    rc = lib.b200tk_linear_gelu_fwd(
+        ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(weight.data_ptr()),
+        None if bias is None else ctypes.c_void_p(bias.data_ptr()),
+        ctypes.c_void_p(out.data_ptr()),
+        DTYPE_CODES[x.dtype], rows, in_features, weight.shape[0],
         _stream_handle(x.device),
     )
     _check(rc)

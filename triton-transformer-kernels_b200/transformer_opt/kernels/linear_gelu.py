@@ -1,0 +1,82 @@
+"""FFN input projection with its exact GELU fused on sm_100a (libb200tk.so).
+
+``fused_linear_gelu(x, weight, bias)`` computes
+``F.gelu(F.linear(x, weight, bias), approximate="none")`` -- the
+``F.gelu(layer.ffn_in(h))`` pair of the reference's block
+(benchmarks/torch_transformer_benchmark.py:131, 141; placed by the fused layer
+loop at transformer_opt/submission.py:506-508) -- as one tcgen05 GEMM whose
+epilogue adds the bias and applies the GELU before the single store.
+
+float32 inputs multiply as TF32 (what an fp32 Linear computes with
+``torch.backends.cuda.matmul.allow_tf32``); float16 / bfloat16 round the
+biased fp32 sum to the input dtype before the GELU, as the unfused Linear's
+output tensor does. Unsupported calls raise ``ValueError``; a missing library
+raises ``RuntimeError``. No fallback.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from transformer_opt.config import SUPPORTED_DTYPES, device_supported
+from transformer_opt.kernels import _native
+
+
+def linear_gelu_unsupported_reason(
+    x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]
+) -> Optional[str]:
+    """Why ``fused_linear_gelu`` would reject these tensors, or None."""
+    if x.device.type != "cuda":
+        return "fused linear GELU requires CUDA tensors"
+    reason = device_supported(x.device)
+    if reason is not None:
+        return reason
+    if x.dtype not in SUPPORTED_DTYPES:
+        return "fused linear GELU supports float32, float16 and bfloat16"
+    if x.ndim < 2:
+        return "x must have rank two or higher"
+    if weight.ndim != 2 or weight.shape[1] != x.shape[-1]:
+        return "weight must be [out_features, in_features] with in_features == x.shape[-1]"
+    if weight.dtype != x.dtype or weight.device != x.device:
+        return "weight must match x's dtype and device"
+    if bias is not None and (
+        bias.shape != (weight.shape[0],) or bias.dtype != x.dtype or bias.device != x.device
+    ):
+        return "bias must be [out_features] with x's dtype and device"
+    if not x.is_contiguous() or not weight.is_contiguous() or (
+        bias is not None and not bias.is_contiguous()
+    ):
+        return "fused linear GELU requires contiguous tensors"
+    elem = x.element_size()
+    if (x.shape[-1] * elem) % 16 or (weight.shape[0] * elem) % 16:
+        return "in_features and out_features must be multiples of 16 bytes of elements"
+    for t in (x, weight, bias):
+        if t is not None and t.data_ptr() % 16:
+            return "tensors must be 16-byte aligned"
+    return None
+
+
+def fused_linear_gelu(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    *,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """``gelu(x @ weight.T + bias)`` (exact erf GELU) on the current stream."""
+    reason = linear_gelu_unsupported_reason(x, weight, bias)
+    if reason is not None:
+        raise ValueError(reason)
+    shape = (*x.shape[:-1], weight.shape[0])
+    if out is None:
+        out = torch.empty(shape, dtype=x.dtype, device=x.device)
+    elif out.shape != shape or out.dtype != x.dtype or out.device != x.device or (
+        not out.is_contiguous() or out.data_ptr() % 16
+    ):
+        raise ValueError("out must be a contiguous, 16-byte aligned tensor of the output shape")
+    if x.numel() == 0:
+        return out
+    _native.linear_gelu_fwd(x, weight, bias, out)
+    return out
