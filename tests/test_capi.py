@@ -101,3 +101,21 @@ def test_residual_layer_norm_validation_errors_need_no_gpu():
     assert b"mask" in lib.b200tk_last_error()
     rc = lib.b200tk_residual_layer_norm_fwd(p, p, p, None, None, p, p, 0, 0, 64, 1e-5, 0, None)
     assert rc == _native.OK  # zero rows: nothing to launch
+
+
+def test_linear_gelu_validation_errors_need_no_gpu():
+    lib = _native.load()
+    p = ctypes.c_void_p(16)
+    # in_features of 6 fp32 = 24 bytes: not a multiple of 16 bytes
+    assert lib.b200tk_linear_gelu_fwd(p, p, None, p, 0, 4, 6, 32, None) == _native.ERR_UNSUPPORTED
+    assert b"16 bytes" in lib.b200tk_last_error()
+    # out_features of 12 bf16 = 24 bytes
+    assert lib.b200tk_linear_gelu_fwd(p, p, None, p, 2, 4, 64, 12, None) == _native.ERR_UNSUPPORTED
+    assert lib.b200tk_linear_gelu_fwd(p, p, None, p, 9, 4, 64, 64, None) == _native.ERR_INVALID_ARGUMENT
+    assert lib.b200tk_linear_gelu_fwd(p, p, None, p, 0, 4, 0, 64, None) == _native.ERR_INVALID_ARGUMENT
+    assert lib.b200tk_linear_gelu_fwd(p, p, None, p, 0, -1, 64, 64, None) == _native.ERR_INVALID_ARGUMENT
+    # misaligned pointer
+    odd = ctypes.c_void_p(24)
+    assert lib.b200tk_linear_gelu_fwd(odd, p, None, p, 0, 4, 64, 64, None) == _native.ERR_UNSUPPORTED
+    # zero rows: nothing to launch
+    assert lib.b200tk_linear_gelu_fwd(p, p, None, p, 0, 0, 64, 64, None) == _native.OK

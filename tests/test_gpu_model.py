@@ -58,10 +58,10 @@ def harness_precision_flags():
     torch.set_float32_matmul_precision(saved[2])
 
 
-def build_pair(shape, dtype, weight_seed=0):
+def build_pair(shape, dtype, weight_seed=0, **kwargs):
     torch.manual_seed(weight_seed)
     baseline = oracle.BaselineTransformer(oracle.TransformerConfig(*shape))
-    optimized = UserOptimizedTransformer(TransformerConfig(*shape))
+    optimized = UserOptimizedTransformer(TransformerConfig(*shape), **kwargs)
     oracle.copy_model_weights(baseline, optimized, strict=True)
     return (
         baseline.to(device="cuda", dtype=dtype).eval(),
@@ -101,10 +101,13 @@ class full_fp32_matmuls:
         torch.backends.cuda.matmul.allow_tf32 = self.saved
 
 
-@pytest.mark.parametrize("name", ["C1", "C2", "C4"])
-def test_model_matches_explicit_baseline_on_five_seeds(name):
+@pytest.mark.parametrize(
+    "name,ffn_backend",
+    [("C1", "auto"), ("C1", "b200"), ("C2", "auto"), ("C2", "torch"), ("C4", "auto")],
+)
+def test_model_matches_explicit_baseline_on_five_seeds(name, ffn_backend):
     shape, dtype = CONFIGS[name]
-    baseline, optimized = build_pair(shape, dtype)
+    baseline, optimized = build_pair(shape, dtype, ffn_backend=ffn_backend)
     cfg = oracle.TransformerConfig(*shape)
     failures = []
     for seed in range(5):
@@ -119,6 +122,9 @@ def test_model_matches_explicit_baseline_on_five_seeds(name):
     layers = shape[5]
     assert optimized.attention_backend_counts["b200"] == 5 * layers
     assert optimized.fused_residual_layer_norm_calls == 10 * layers
+    # C1's FFN projection (256 x 1024 outputs) is below the auto threshold
+    fused_ffn = ffn_backend == "b200" or (ffn_backend == "auto" and name != "C1")
+    assert optimized.fused_linear_gelu_calls == (5 * layers if fused_ffn else 0)
     assert not failures, failures
     assert _native.device_status(0) == 0
 
@@ -139,6 +145,7 @@ def test_c5_bf16_model_error_budget_parity_on_five_seeds():
         print(f"C5 seed {seed}: {stats}")
         del ref, out, exact
     assert optimized.attention_backend_counts["b200"] == 5 * shape[5]
+    assert optimized.fused_linear_gelu_calls == 5 * shape[5]
     assert _native.device_status(0) == 0
 
 

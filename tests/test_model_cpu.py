@@ -89,6 +89,24 @@ def test_constructor_validation():
         UserOptimizedTransformer(cfg, execution_mode="never")
     for mode in ("auto", "eager", "graph"):
         assert UserOptimizedTransformer(cfg, execution_mode=mode).execution_mode == mode
+    with pytest.raises(ValueError, match="ffn_backend"):
+        UserOptimizedTransformer(cfg, ffn_backend="cublaslt")
+    for backend in ("auto", "b200", "torch"):
+        model = UserOptimizedTransformer(cfg, ffn_backend=backend)
+        assert model.ffn_backend == backend and model.fused_linear_gelu_calls == 0
+
+
+def test_ffn_backend_is_keyword_only_and_cpu_forward_ignores_it():
+    cfg = TransformerConfig(1, 8, 16, 2, 32, 1, False)
+    with pytest.raises(TypeError):
+        UserOptimizedTransformer(cfg, "auto", "auto", "torch")
+    x = torch.randn(1, 8, 16)
+    fused = UserOptimizedTransformer(cfg, ffn_backend="b200").eval()
+    plain = UserOptimizedTransformer(cfg, ffn_backend="torch").eval()
+    plain.load_state_dict(fused.state_dict(), strict=True)
+    with torch.inference_mode():
+        assert torch.equal(fused(x), plain(x))
+    assert fused.fused_linear_gelu_calls == 0  # CPU: explicit forward, no kernel
 
 
 def test_graph_mode_on_cpu_runs_the_explicit_forward():

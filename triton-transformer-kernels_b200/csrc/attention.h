@@ -65,10 +65,12 @@ struct RlnArgs {
 cudaError_t launch_residual_layer_norm(const RlnArgs& args, cudaStream_t stream);
 
 // Linear + exact GELU (the FFN input projection). Tensor maps are built by
-// the host: x [rows, k_in] and weight [n_out, k_in], both row-major.
+// the host: x [rows, k_in], weight [n_out, k_in] and out [rows, n_out], all
+// row-major.
 struct LinearGeluArgs {
   alignas(64) unsigned char tm_x[128];
   alignas(64) unsigned char tm_w[128];
+  alignas(64) unsigned char tm_out[128];
   const void* bias;
   void* out;
   int64_t rows, k_in, n_out;

@@ -356,6 +356,7 @@ int b200tk_linear_gelu_fwd(const void* x, const void* weight, const void* bias, 
   std::memset(&a, 0, sizeof(a));
   int rc = encode_matrix_map(a.tm_x, x, rows, in_features, dtype, 128);
   if (rc == B200TK_OK) rc = encode_matrix_map(a.tm_w, weight, out_features, in_features, dtype, 128);
+  if (rc == B200TK_OK) rc = encode_matrix_map(a.tm_out, out, rows, out_features, dtype, 32);
   if (rc != B200TK_OK) return rc;
   rc = status_address(&a.status);
   if (rc != B200TK_OK) return rc;

@@ -34,7 +34,9 @@
 //   warps 2-9   epilogue (both CTAs, own 128 rows): tcgen05.ld of the
 //               accumulator (warp w reads TMEM lane quarter w % 4; warps 2-5
 //               take columns 0-127, warps 6-9 columns 128-255), bias,
-//               rounding, GELU, 16-byte stores straight from registers.
+//               rounding, GELU, then a swizzled staging tile in shared memory
+//               and a TMA store (32 rows x 128 bytes), so global memory sees
+//               whole lines instead of 16-byte pieces of 32 rows.
 // Tiles are walked in groups of kGroup row tiles: the pairs in flight share
 // a few row bands of x and a stretch of the weight matrix in L2.
 #include <cuda.h>
@@ -59,10 +61,17 @@ constexpr int kStages = 6;          // smem ring depth
 constexpr int kABytes = BM * 128;   // a 128-byte K slice of this CTA's x rows
 constexpr int kBBytes = kHalfN * 128;  // a 128-byte K slice of its weight rows
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 8;                  // 2 per TMEM lane quarter
+constexpr int kColGroups = kEpiWarps / 4;      // column groups of a lane quarter
+constexpr int kColsPerWarp = BN / kColGroups;  // accumulator columns per epilogue warp
+constexpr int kChunks = kColsPerWarp / 32;     // 32-column TMEM loads per warp and tile
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr int kTmemCols = 2 * BN;  // two accumulators
-constexpr int kBarOff = kStages * kStageBytes;
+// Output staging: per epilogue warp one 32-row x 128-byte tile (128-byte
+// swizzle), stored to global memory by TMA.
+constexpr int kStagingBytes = 32 * 128;
+constexpr int kStagingOff = kStages * kStageBytes;
+constexpr int kBarOff = kStagingOff + kEpiWarps * kStagingBytes;
 constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers and slots, alignment slack
 constexpr int kGroup = 8;                         // pair row tiles per raster group
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -73,6 +82,7 @@ static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 struct __align__(64) LgParams {
   CUtensorMap tm_x;  // [rows, k] row-major, box {128 bytes, BM rows}
   CUtensorMap tm_w;  // [n, k] row-major, box {128 bytes, kHalfN rows}
+  CUtensorMap tm_out;  // [rows, n] row-major, box {128 bytes, 32 rows}
   const void* bias;  // [n] or nullptr
   void* out;         // [rows, n] row-major
   int64_t rows;
@@ -141,34 +151,6 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   } else {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
-  }
-}
-
-// Store 32 consecutive outputs of one row starting at column cb: 16-byte
-// stores when the chunk lies inside the matrix, masked scalar stores at the
-// right edge.
-template <typename T>
-__device__ __forceinline__ void store32(T* orow, int cb, int n_out, const float (&v)[32]) {
-  if (cb + 32 <= n_out) {
-    if constexpr (std::is_same_v<T, float>) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(orow + cb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; j += 8)
-        *reinterpret_cast<uint4*>(orow + cb + j) =
-            make_uint4(pack2<T>(v[j], v[j + 1]), pack2<T>(v[j + 2], v[j + 3]),
-                       pack2<T>(v[j + 4], v[j + 5]), pack2<T>(v[j + 6], v[j + 7]));
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (cb + j < n_out) {
-        if constexpr (std::is_same_v<T, float>) orow[cb + j] = v[j];
-        else if constexpr (std::is_same_v<T, __half>) orow[cb + j] = __float2half_rn(v[j]);
-        else orow[cb + j] = __float2bfloat16_rn(v[j]);
-      }
   }
 }
 
@@ -360,32 +342,39 @@ __global__ void __launch_bounds__(kThreads, 1) linear_gelu_kernel(const __grid_c
     }
   } else {
     // ----------------------------------------------------------- epilogue
+    // Each 32-column chunk: TMEM -> registers (bias, rounding, GELU) ->
+    // this warp's staging tile in shared memory -> TMA store. A staging row
+    // holds 128 bytes (32 fp32 or 64 16-bit outputs of one tile row), so
+    // fp32 stores every chunk and 16-bit every second one. Rows and columns
+    // outside the matrix are clipped by the store.
     const int quarter = warp & 3;         // TMEM lanes this warp may read
-    const int half = (warp - 2) >> 2;     // columns [128 * half, 128 * half + 128)
+    const int group = (warp - 2) >> 2;    // columns [group, group + 1) * kColsPerWarp
     const int row = quarter * 32 + lane;  // CTA tile row == TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t acc_empty_leader = mapa_shared(bar_acc_empty(0), 0);
+    const uint32_t staging = sbase + kStagingOff + (warp - 2) * kStagingBytes;
+    const uint32_t srow = staging + lane * 128;  // this lane's staging row
+    constexpr bool kWide = std::is_same_v<T, float>;  // 32 outputs fill a staging row
     const T* bias = static_cast<const T*>(p.bias);
+    if (lane == 0) tma_prefetch_desc(&p.tm_out);
     int tc = 0;
     for (int t = pair; t < total; t += npairs, ++tc) {
       int m, n;
       tile_coords(t, m, n);
       const int buf = tc & 1;
-      const int col0 = n * BN + half * 128;  // first column of this warp's half
-      // The bias of the warp's 128 columns, four per lane (lane l holds
-      // columns col0 + 4l .. 4l + 3), is fetched before the accumulator wait
-      // so that its latency hides behind it; the chunks read it by shuffle.
+      const int col0 = n * BN + group * kColsPerWarp;  // first column of this warp
+      // The bias of the warp's columns, four per lane (lane l holds columns
+      // col0 + 4l .. 4l + 3), is fetched before the accumulator wait so that
+      // its latency hides behind it; the chunks read it by shuffle.
       float bl[4] = {0.f, 0.f, 0.f, 0.f};
-      if (bias != nullptr && col0 + 4 * lane < p.n_out) load_bias4(bias + col0 + 4 * lane, bl);
+      if (bias != nullptr && 4 * lane < kColsPerWarp && col0 + 4 * lane < p.n_out)
+        load_bias4(bias + col0 + 4 * lane, bl);
       if (!__all_sync(0xFFFFFFFFu, wait(bar_acc_full(buf), (tc >> 1) & 1))) break;
       tc_fence_after();
-      const int64_t grow = static_cast<int64_t>(m) * 2 * BM + rank * BM + row;
-      T* orow = static_cast<T*>(p.out) + grow * p.n_out;
-      const bool row_ok = grow < p.rows;
-      // bias, rounding, GELU and store of the 32 columns held in r
+      const int row0 = m * 2 * BM + static_cast<int>(rank) * BM + quarter * 32;  // warp's first row
+      // bias, rounding, GELU, staging and (when a staging row is full) the
+      // store of the 32 columns held in r
       auto chunk = [&](const uint32_t(&r)[32], int c) {
-        const int cb = col0 + c * 32;
-        if (cb >= p.n_out) return;  // warp-uniform
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -395,32 +384,72 @@ __global__ void __launch_bounds__(kThreads, 1) linear_gelu_kernel(const __grid_c
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = gelu_erf(round_to<T>(v[j]));
-        if (row_ok) store32<T>(orow, cb, p.n_out, v);
+        // the staging tile is free once the previous store has read it
+        if (kWide || (c & 1) == 0) {
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+        }
+        // 16-byte unit u of the row goes to unit u ^ (row % 8) (128-byte
+        // swizzle, conflict-free across the 8 lanes of a store phase)
+        if constexpr (kWide) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t dst = srow + ((u ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(v[4 * u]),
+                         "f"(v[4 * u + 1]), "f"(v[4 * u + 2]), "f"(v[4 * u + 3])
+                         : "memory");
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int u = 4 * (c & 1) + k;
+            const uint32_t dst = srow + ((u ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst),
+                         "r"(pack2<T>(v[8 * k], v[8 * k + 1])),
+                         "r"(pack2<T>(v[8 * k + 2], v[8 * k + 3])),
+                         "r"(pack2<T>(v[8 * k + 4], v[8 * k + 5])),
+                         "r"(pack2<T>(v[8 * k + 6], v[8 * k + 7]))
+                         : "memory");
+          }
+        }
+        if (kWide || (c & 1) == 1) {
+          const int cs = col0 + (kWide ? c : c - 1) * 32;  // first column of the staging row
+          fence_proxy_async_smem();  // staging writes -> visible to the TMA store
+          __syncwarp();
+          if (lane == 0 && cs < p.n_out && row0 < p.rows) {
+            tma_store_2d(&p.tm_out, staging, cs, row0);
+            bulk_commit_group();
+          }
+        }
       };
       // Accumulator chunks of 32 columns: chunk c + 1 is loaded from TMEM
       // while chunk c is computed (two register sets, ra / rb).
-      const uint32_t acc = lane_base + buf * BN + half * 128;
+      const uint32_t acc = lane_base + buf * BN + group * kColsPerWarp;
       uint32_t ra[32], rb[32];
       tmem_ld32(acc, ra);
       tc_wait_ld_regs(ra);
 #pragma unroll 1
-      for (int cp = 0; cp < 2; ++cp) {
+      for (int cp = 0; cp < kChunks / 2; ++cp) {
+        const bool last = cp + 1 == kChunks / 2;
         tmem_ld32(acc + (2 * cp + 1) * 32, rb);
         chunk(ra, 2 * cp);
         tc_wait_ld_regs(rb);
-        if (cp == 0) {
-          tmem_ld32(acc + 64, ra);
+        if (!last) {
+          tmem_ld32(acc + (2 * cp + 2) * 32, ra);
         } else {
           // every chunk is in registers: the leader's MMA may reuse the
           // accumulator (in both CTAs) once both epilogues have arrived
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(acc_empty_leader + 8 * buf);
+          if (lane == 0) mbar_arrive_remote(acc_empty_leader + 8 * buf);
         }
         chunk(rb, 2 * cp + 1);
-        if (cp == 0) tc_wait_ld_regs(ra);
+        if (!last) tc_wait_ld_regs(ra);
       }
     }
+    // every output store has completed before the CTA exits
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   // ------------------------------------------------------------- teardown
@@ -498,6 +527,7 @@ cudaError_t launch_linear_gelu(const LinearGeluArgs& a, cudaStream_t stream) {
   lg::LgParams prm;
   prm.tm_x = *reinterpret_cast<const CUtensorMap*>(a.tm_x);
   prm.tm_w = *reinterpret_cast<const CUtensorMap*>(a.tm_w);
+  prm.tm_out = *reinterpret_cast<const CUtensorMap*>(a.tm_out);
   prm.bias = a.bias;
   prm.out = a.out;
   prm.rows = a.rows;

@@ -15,10 +15,16 @@ replays only launch-bound forwards (AUTO_GRAPH_MAX_ELEMENTS).
 On an sm_100 GPU in inference mode every layer runs
   packed QKV projection (cuBLAS, fp32) or three projections (16-bit)
   -> fused attention (libb200tk, tcgen05)  -> out_proj (cuBLAS)
-  -> fused residual + norm2 (libb200tk)    -> FFN (cuBLAS + GELU)
+  -> fused residual + norm2 (libb200tk)
+  -> ffn_in + exact GELU (libb200tk, one tcgen05 GEMM with the GELU in its
+     epilogue)                              -> ffn_out (cuBLAS)
   -> fused residual + next norm1 / final_norm (libb200tk)
 which is the reference's fused layer loop (:481-525) applied to every shape
-and dtype instead of four measured rows. Everything else (CPU, autograd,
+and dtype instead of four measured rows. ffn_backend ("auto" | "b200" |
+"torch") picks the FFN input projection: the fused kernel ("auto": where it
+applies and the output has at least FUSED_FFN_MIN_OUTPUTS elements; fp32
+only while TF32 matmuls are allowed, the precision the unfused fp32 Linear
+then has), or cuBLAS + ATen GELU. Everything else (CPU, autograd,
 training mode, backends other than the custom one) runs the explicit
 PyTorch forward with attention through ``attention_forward``.
 """
@@ -42,6 +48,7 @@ from transformer_opt.config import (
 )
 from transformer_opt.dispatch import attention_forward
 from transformer_opt.kernels import _native
+from transformer_opt.kernels.linear_gelu import fused_linear_gelu, linear_gelu_unsupported_reason
 from transformer_opt.kernels.residual_layer_norm import fused_residual_layer_norm, layer_norm
 from transformer_opt.model import (
     SelfAttentionWeights,
@@ -52,6 +59,11 @@ from transformer_opt.model import (
 )
 
 EXECUTION_MODES = ("auto", "eager", "graph")
+FFN_BACKENDS = ("auto", "b200", "torch")
+# ffn_backend="auto" fuses the FFN input projection with its GELU when the
+# projection has at least this many output elements (rows * ffn_dim); below
+# it the launch and the CTA-pair set-up outweigh the saved GELU pass.
+FUSED_FFN_MIN_OUTPUTS = 1 << 22
 # "auto" replays a CUDA graph when the forward is launch-bound: at most this
 # many activation elements (batch * seq * d_model) times layers. Larger
 # forwards keep the GPU busy without one, and replay would add an input copy
@@ -75,6 +87,8 @@ class UserOptimizedTransformer(TransformerWeights):
         config: TransformerConfig,
         attention_backend: str = "auto",
         execution_mode: str = "auto",
+        *,
+        ffn_backend: str = "auto",
     ) -> None:
         super().__init__(config)
         if attention_backend not in ATTENTION_BACKENDS:
@@ -84,8 +98,11 @@ class UserOptimizedTransformer(TransformerWeights):
             )
         if execution_mode not in EXECUTION_MODES:
             raise ValueError(f"execution_mode must be one of {EXECUTION_MODES}")
+        if ffn_backend not in FFN_BACKENDS:
+            raise ValueError(f"ffn_backend must be one of {FFN_BACKENDS}, got {ffn_backend!r}")
         self.attention_backend = attention_backend
         self.execution_mode = execution_mode
+        self.ffn_backend = ffn_backend
         self._lock = threading.RLock()
         self.attention_backend_counts: Dict[str, int] = {
             CUSTOM_BACKEND: 0,
@@ -93,6 +110,7 @@ class UserOptimizedTransformer(TransformerWeights):
             "reference": 0,
         }
         self.fused_residual_layer_norm_calls = 0
+        self.fused_linear_gelu_calls = 0
         self.cuda_graph_replays = 0
         self._graph: Optional["_ForwardGraph"] = None
         self._host_streams: Dict[int, Tuple[torch.cuda.Stream, ...]] = {}
@@ -104,6 +122,7 @@ class UserOptimizedTransformer(TransformerWeights):
     def reset_attention_backend_counts(self) -> None:
         self.attention_backend_counts = {CUSTOM_BACKEND: 0, "sdpa": 0, "reference": 0}
         self.fused_residual_layer_norm_calls = 0
+        self.fused_linear_gelu_calls = 0
         self.cuda_graph_replays = 0
 
     def __getstate__(self):
@@ -117,6 +136,8 @@ class UserOptimizedTransformer(TransformerWeights):
     def __setstate__(self, state):
         super().__setstate__(state)
         self._lock = threading.RLock()
+        self.__dict__.setdefault("ffn_backend", "auto")
+        self.__dict__.setdefault("fused_linear_gelu_calls", 0)
 
     def _apply(self, fn, recurse=True):
         # device / dtype moves invalidate the packed projection weights and
@@ -387,7 +408,8 @@ class UserOptimizedTransformer(TransformerWeights):
             m.eps for m in self.modules() if isinstance(m, nn.LayerNorm)
         )
         return (
-            tuple(params), norms, self.attention_backend, x.device, tuple(x.shape), x.dtype,
+            tuple(params), norms, self.attention_backend, self.ffn_backend, x.device,
+            tuple(x.shape), x.dtype,
             valid_token_mask is not None, torch.backends.cuda.matmul.allow_tf32,
             torch.is_inference_mode_enabled(),  # static buffers are inference tensors or not
         )
@@ -403,6 +425,7 @@ class UserOptimizedTransformer(TransformerWeights):
             for backend, count in graph.backend_counts.items():
                 self.attention_backend_counts[backend] += count
             self.fused_residual_layer_norm_calls += graph.fused_calls
+            self.fused_linear_gelu_calls += graph.ffn_calls
             self.cuda_graph_replays += 1
             return out
 
@@ -425,6 +448,22 @@ class UserOptimizedTransformer(TransformerWeights):
         self.fused_residual_layer_norm_calls += 1
         return residual, normalized
 
+    def _ffn_in_gelu(self, linear: nn.Linear, h: torch.Tensor) -> torch.Tensor:
+        """``F.gelu(linear(h), approximate="none")``, fused into one kernel
+        where ffn_backend allows it (reference: submission.py:506-508)."""
+        if self.ffn_backend != "torch" and (
+            h.dtype != torch.float32 or torch.backends.cuda.matmul.allow_tf32
+        ):
+            reason = linear_gelu_unsupported_reason(h, linear.weight, linear.bias)
+            if reason is None:
+                outputs = (h.numel() // h.shape[-1]) * linear.out_features
+                if self.ffn_backend == "b200" or outputs >= FUSED_FFN_MIN_OUTPUTS:
+                    self.fused_linear_gelu_calls += 1
+                    return fused_linear_gelu(h, linear.weight, linear.bias)
+            elif self.ffn_backend == "b200":
+                raise ValueError(f"ffn_backend='b200' cannot run this projection: {reason}")
+        return F.gelu(linear(h), approximate="none")
+
     def _forward_fused(
         self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
     ) -> torch.Tensor:
@@ -436,7 +475,7 @@ class UserOptimizedTransformer(TransformerWeights):
             del normalized
             x, ffn_input = self._fused_residual_norm(x, attn_out, layer.norm2, valid_token_mask)
             del attn_out
-            ffn_out = layer.ffn_out(F.gelu(layer.ffn_in(ffn_input), approximate="none"))
+            ffn_out = layer.ffn_out(self._ffn_in_gelu(layer.ffn_in, ffn_input))
             del ffn_input
             is_last = index + 1 == len(self.layers)
             next_norm = self.final_norm if is_last else self.layers[index + 1].norm1
@@ -475,6 +514,7 @@ class _ForwardGraph:
         self.mask = valid_token_mask.clone() if valid_token_mask is not None else None
         counts_before = dict(model.attention_backend_counts)
         fused_before = model.fused_residual_layer_norm_calls
+        ffn_before = model.fused_linear_gelu_calls
         stream = torch.cuda.Stream(device=x.device)
         current = torch.cuda.current_stream(x.device)
         stream.wait_stream(current)
@@ -486,6 +526,7 @@ class _ForwardGraph:
             current.wait_stream(stream)
             capture_counts = dict(model.attention_backend_counts)
             capture_fused = model.fused_residual_layer_norm_calls
+            capture_ffn = model.fused_linear_gelu_calls
             self.graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graph, stream=stream):
                 self.out = model._forward_fused(self.x, self.mask)
@@ -494,6 +535,7 @@ class _ForwardGraph:
                 k: v - capture_counts[k] for k, v in model.attention_backend_counts.items()
             }
             self.fused_calls = model.fused_residual_layer_norm_calls - capture_fused
+            self.ffn_calls = model.fused_linear_gelu_calls - capture_ffn
             # keep the packed weights the graph reads alive
             self.packed = tuple(model._packed_qkv_cache.values())
             self.done = torch.cuda.Event()
@@ -502,6 +544,7 @@ class _ForwardGraph:
             # warm-up and capture are set-up, not user-visible forwards
             model.attention_backend_counts = counts_before
             model.fused_residual_layer_norm_calls = fused_before
+            model.fused_linear_gelu_calls = ffn_before
 
     def replay(self, x, valid_token_mask) -> torch.Tensor:
         current = torch.cuda.current_stream(x.device)
