@@ -167,17 +167,41 @@ class ClockSampler:
         }
 
 
+def ffn_summary(ms, flops, launches_per_step, dtype, peaks):
+    """Roofline of the fused FFN input projection + GELU (one GEMM per layer)."""
+    if launches_per_step == 0:
+        return {"fused": False}
+    achieved = flops / (ms / 1000.0) / 1e12
+    # TF32 (fp32 inputs) runs at half the bf16 tensor rate
+    peak = peaks["bf16_tflops_sustained"] / (2.0 if dtype == torch.float32 else 1.0)
+    return {
+        "fused": True,
+        "bound": "tensor",
+        "kernel": "linear_gelu_kernel (tcgen05 cta_group::2 GEMM + bias + erf GELU epilogue)",
+        "launches_per_step": launches_per_step,
+        "launch_ms": ms,
+        "flops_per_launch": flops,
+        "achieved": achieved,
+        "peak": peak,
+        "unit": "TFLOP/s",
+        "frac": achieved / peak,
+        "peak_source": f"{peaks['source']} bf16_tflops_sustained"
+        + (" / 2 (TF32)" if dtype == torch.float32 else ""),
+    }
+
+
 class LaunchTimer:
     """CUDA-event timing of each libb200tk launch on the stream it runs on."""
 
     def __init__(self) -> None:
         self.enabled = False
-        self.pairs = {"attention": [], "rln": []}
+        self.pairs = {"attention": [], "rln": [], "ffn": []}
         self.launches = 0
 
     def wrap(self, native):
         timer = self
         orig_attn, orig_rln = native.attention_fwd, native.residual_layer_norm_fwd
+        orig_ffn = native.linear_gelu_fwd
 
         def timed(kind, fn):
             def inner(*args, **kwargs):
@@ -191,17 +215,25 @@ class LaunchTimer:
                 end.record()
                 # keep sizes only: holding the tensors would pin every step's activations
                 x = args[0]
-                meta = (x.numel(), x.element_size(), x.shape[-1], args[1] is None)
+                if kind == "ffn":
+                    meta = (x.numel() // x.shape[-1], x.shape[-1], args[1].shape[0])
+                else:
+                    meta = (x.numel(), x.element_size(), x.shape[-1], args[1] is None)
                 timer.pairs[kind].append((start, end, meta))
                 return result
             return inner
 
         native.attention_fwd = timed("attention", orig_attn)
         native.residual_layer_norm_fwd = timed("rln", orig_rln)
+        native.linear_gelu_fwd = timed("ffn", orig_ffn)
 
     def mean_ms(self, kind: str) -> float:
         times = [s.elapsed_time(e) for s, e, _ in self.pairs[kind]]
         return sum(times) / len(times) if times else float("nan")
+
+    def ffn_flops_per_launch(self) -> float:
+        total = sum(2.0 * rows * k * n for _, _, (rows, k, n) in self.pairs["ffn"])
+        return total / max(1, len(self.pairs["ffn"]))
 
     def rln_bytes_per_launch(self) -> float:
         total = 0.0
@@ -436,6 +468,9 @@ def run_b200_arm(args) -> int:
         attn_ms = timer.mean_ms("attention")
         rln_ms = timer.mean_ms("rln")
         rln_bytes = timer.rln_bytes_per_launch()
+        ffn_ms = timer.mean_ms("ffn")
+        ffn_flops = timer.ffn_flops_per_launch()
+        ffn_launches = len(timer.pairs["ffn"]) // max(1, args.steps)
 
         # ---- end-to-end through the public API with host buffers
         x_host = x.cpu().pin_memory()
@@ -538,6 +573,7 @@ def run_b200_arm(args) -> int:
             "launch_ms": rln_ms,
             "bytes_per_launch": rln_bytes,
         },
+        "ffn_in_gelu": ffn_summary(ffn_ms, ffn_flops, ffn_launches, dtype, peaks),
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "validation": {

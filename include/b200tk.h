@@ -52,6 +52,7 @@ extern "C" {
 #define B200TK_RLN_ZERO_INVALID_RESIDUAL 1u   /* residual_out row := 0 where mask is false */
 #define B200TK_RLN_ZERO_INVALID_NORMALIZED 2u /* normalized_out row := 0 where mask is false */
 #define B200TK_RLN_NO_UPDATE 4u               /* plain LayerNorm: update and residual_out unused */
+#define B200TK_RLN_ROUND_TF32 8u              /* float32: normalized_out rounded to TF32 (see below) */
 
 /* Device status bits (b200tk_device_status). */
 #define B200TK_STATUS_PIPELINE_TIMEOUT 1u /* an mbarrier wait hit its iteration/time limit */
@@ -112,6 +113,10 @@ B200TK_API int b200tk_attention_route(const void* q, const int64_t* q_strides, c
  * with fp32 statistics. With valid_mask (one bool per row) and the
  * B200TK_RLN_ZERO_* flags, invalid rows are zeroed in the chosen outputs.
  * B200TK_RLN_NO_UPDATE turns the call into a plain LayerNorm of x.
+ * B200TK_RLN_ROUND_TF32 (float32 only) rounds normalized_out to the nearest
+ * TF32 value (10 mantissa bits, ties away from zero) -- the operand rounding
+ * of a TF32 matmul, done once here for a consumer whose tensor cores read
+ * the operand as stored (b200tk_linear_gelu_fwd).
  *
  * Replaces: transformer_opt/kernels/residual_layer_norm.py:159-238
  * (fused_residual_layer_norm, launching _residual_layer_norm_fwd at :73-126).
@@ -138,9 +143,12 @@ B200TK_API int b200tk_residual_layer_norm_fwd(const void* x, const void* update,
  * x      : [rows, in_features] row-major.   weight : [out_features, in_features]
  *          row-major (nn.Linear layout).     bias : [out_features] or NULL.
  * out    : [rows, out_features] row-major, in `dtype`.
- * Accumulation and bias are fp32. float32 multiplies as TF32 (the precision of
- * an fp32 matmul with TF32 allowed); float16/bfloat16 round the biased sum to
- * dtype before the GELU, as the unfused Linear's output tensor does.
+ * Accumulation and bias are fp32. float32 multiplies as TF32: the tensor
+ * cores read the top 19 bits of each operand (they truncate), so callers
+ * matching a round-to-nearest TF32 matmul pass x and weight already rounded
+ * (B200TK_RLN_ROUND_TF32 for x; the weight once, when it is loaded).
+ * float16/bfloat16 round the biased sum to dtype before the GELU, as the
+ * unfused Linear's output tensor does.
  * in_features and out_features must be multiples of 16 bytes of elements and
  * every pointer 16-byte aligned (B200TK_ERR_UNSUPPORTED otherwise).
  */

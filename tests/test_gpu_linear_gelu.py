@@ -11,7 +11,9 @@ Three kinds of check:
     16-bit rounding of the Linear's output), on ragged rows, ragged K
     stages, ragged column tiles and a persistent multi-tile case;
   * fp32 against the unfused oracle (cuBLAS TF32 Linear + ATen GELU) with the
-    harness rule, abs_err <= 1e-3 OR abs_err <= 1e-2 * |ref|.
+    harness rule, abs_err <= 1e-3 OR abs_err <= 1e-2 * |ref|;
+  * fp32 with operands rounded to TF32 beforehand (what the model feeds it)
+    against cuBLAS TF32 + ATen GELU within fp32 accumulation-order error.
 """
 
 from __future__ import annotations
@@ -160,3 +162,23 @@ def test_unsupported_shapes_raise_value_error():
         fused_linear_gelu(x, w, None)
     with pytest.raises(ValueError):
         fused_linear_gelu(x.cpu(), w.cpu(), None)
+
+
+def _round_tf32(t: torch.Tensor) -> torch.Tensor:
+    """Nearest TF32 values (ties away from zero), as fp32."""
+    return ((t.contiguous().view(torch.int32) + 0x1000) & -0x2000).view(torch.float32)
+
+
+@pytest.mark.parametrize("rows,k,n", [(4096, 1024, 4096), (1024, 4096, 16384)])
+def test_fp32_with_tf32_rounded_operands_matches_cublas_tf32(rows, k, n):
+    """With operands rounded to TF32 beforehand, every product is the one a
+    TF32 cuBLAS matmul forms, so the fused result differs from cuBLAS TF32 +
+    ATen GELU only by fp32 accumulation order (the model relies on this)."""
+    x, w, b = _inputs(rows, k, n, torch.float32, seed=13)
+    x, w = _round_tf32(x), _round_tf32(w)
+    out = fused_linear_gelu(x, w, b)
+    ref = oracle.linear_gelu(x, w, b)  # cuBLAS TF32 Linear + ATen GELU
+    mag = x.abs() @ w.abs().t()
+    tol = GELU_SLOPE * (k * 2.0 ** -22) * mag + 2.0 ** -21 * ref.abs() + 1e-7
+    err = (out - ref).abs()
+    assert (err <= tol).all(), f"worst excess {(err - tol).max().item():.3g}"

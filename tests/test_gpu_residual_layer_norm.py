@@ -142,3 +142,24 @@ def test_baseline_config_rows_full_size(rows, width, dtype):
     nf = n.float()
     assert nf.mean(dim=-1).abs().max().item() < 2e-2
     assert (nf.var(dim=-1, unbiased=False) - 1).abs().max().item() < 2e-2
+
+
+def test_round_normalized_tf32_flag():
+    """ROUND_TF32: normalized output = nearest TF32 value (ties away from
+    zero) of the unrounded output; the residual is unchanged; fp32 only."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    for rows, width in ((300, 1024), (7, 1001)):  # vector path, scalar path
+        x = torch.randn(rows, width, device="cuda", generator=g)
+        u = torch.randn(rows, width, device="cuda", generator=g)
+        w = torch.randn(width, device="cuda", generator=g)
+        b = torch.randn(width, device="cuda", generator=g)
+        r0, n0 = fused_residual_layer_norm(x, u, w, b, 1e-5)
+        r1, n1 = fused_residual_layer_norm(x, u, w, b, 1e-5, round_normalized_tf32=True)
+        expect = ((n0.view(torch.int32) + 0x1000) & -0x2000).view(torch.float32)
+        assert torch.equal(r0, r1)
+        assert torch.equal(n1, expect)
+        assert not torch.equal(n0, n1)
+    xb = torch.randn(4, 64, device="cuda", dtype=torch.bfloat16)
+    wb = torch.ones(64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        fused_residual_layer_norm(xb, xb, wb, None, 1e-5, round_normalized_tf32=True)

@@ -307,7 +307,9 @@ int b200tk_residual_layer_norm_fwd(const void* x, const void* update, const void
   if (rows < 0 || width <= 0) return fail(B200TK_ERR_INVALID_ARGUMENT, "rows >= 0 and width > 0");
   if (width > 65536)
     return fail(B200TK_ERR_UNSUPPORTED, "normalized feature dimension exceeds the fused kernel limit");
-  if (flags & ~7u) return fail(B200TK_ERR_INVALID_ARGUMENT, "unknown flag bits");
+  if (flags & ~15u) return fail(B200TK_ERR_INVALID_ARGUMENT, "unknown flag bits");
+  if ((flags & B200TK_RLN_ROUND_TF32) && dtype != B200TK_DTYPE_FLOAT32)
+    return fail(B200TK_ERR_INVALID_ARGUMENT, "TF32 rounding applies to float32 only");
   if ((flags & 3u) && valid_mask == nullptr)
     return fail(B200TK_ERR_INVALID_ARGUMENT, "invalid-row zeroing requires valid_token_mask");
   if (rows == 0) return B200TK_OK;

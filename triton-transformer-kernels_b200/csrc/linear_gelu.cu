@@ -57,11 +57,17 @@ namespace lg {
 constexpr int BM = 128;             // rows per CTA (a pair tile has 2 * BM)
 constexpr int BN = 256;             // output features per tile (MMA N)
 constexpr int kHalfN = BN / 2;      // weight rows each CTA of the pair stages
-constexpr int kStages = 6;          // smem ring depth
+#ifndef B200TK_LG_STAGES
+#define B200TK_LG_STAGES 6
+#endif
+#ifndef B200TK_LG_EPI_WARPS
+#define B200TK_LG_EPI_WARPS 8
+#endif
+constexpr int kStages = B200TK_LG_STAGES;  // smem ring depth
 constexpr int kABytes = BM * 128;   // a 128-byte K slice of this CTA's x rows
 constexpr int kBBytes = kHalfN * 128;  // a 128-byte K slice of its weight rows
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kEpiWarps = 8;                  // 2 per TMEM lane quarter
+constexpr int kEpiWarps = B200TK_LG_EPI_WARPS;  // 2 or 4 per TMEM lane quarter
 constexpr int kColGroups = kEpiWarps / 4;      // column groups of a lane quarter
 constexpr int kColsPerWarp = BN / kColGroups;  // accumulator columns per epilogue warp
 constexpr int kChunks = kColsPerWarp / 32;     // 32-column TMEM loads per warp and tile

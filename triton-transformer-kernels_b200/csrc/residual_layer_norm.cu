@@ -7,6 +7,8 @@
 //   mean = sum(r) / width; var = sum((r - mean)^2) / width   (fp32, two-pass)
 //   n = (r - mean) * rsqrt(var + eps) * weight + bias
 //   n = 0            where the row is invalid and ZERO_INVALID_NORMALIZED
+//   n = tf32(n)      with ROUND_TF32 (float32): nearest TF32 value, ties away
+//                    from zero, for a tensor-core consumer that truncates
 // and writes both r and n. The row lives in registers between the passes, so
 // HBM sees exactly one read of x, update and one write of r, n (the roofline
 // minimum of 4 * width * sizeof(T) bytes per row).
@@ -29,6 +31,13 @@
 
 namespace b200tk {
 namespace {
+
+// Nearest TF32 value (10 mantissa bits, ties away from zero) as an fp32.
+__device__ __forceinline__ float round_tf32(float v) {
+  uint32_t u;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(v));
+  return __uint_as_float(u);
+}
 
 template <typename T>
 __device__ __forceinline__ float ld_f32(const T* p) {
@@ -152,6 +161,7 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256)
   if (a.mask != nullptr && row_in) valid = a.mask[row] != 0;
   const bool zero_res = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_RESIDUAL);
   const bool zero_norm = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_NORMALIZED);
+  const bool tf32 = std::is_same_v<T, float> && (a.flags & B200TK_RLN_ROUND_TF32);
 
   const uint4* xv = reinterpret_cast<const uint4*>(static_cast<const T*>(a.x) + row * a.width);
   const uint4* uv = reinterpret_cast<const uint4*>(static_cast<const T*>(a.update) + row * a.width);
@@ -213,6 +223,7 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256)
     for (int e = 0; e < EPV; ++e) {
       const float nrm = (r[i][e] - mean) * rstd * fw[e];
       o[e] = zero_norm ? 0.f : (bp != nullptr ? nrm + fb[e] : nrm);
+      if (tf32) o[e] = round_tf32(o[e]);
     }
     nv[vi] = IO::pack(o);
   }
@@ -229,6 +240,7 @@ __global__ void __launch_bounds__(256) rln_scalar_kernel(const RlnArgs a) {
   if (a.mask != nullptr) valid = a.mask[row] != 0;
   const bool zero_res = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_RESIDUAL);
   const bool zero_norm = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_NORMALIZED);
+  const bool tf32 = std::is_same_v<T, float> && (a.flags & B200TK_RLN_ROUND_TF32);
   const T* x = static_cast<const T*>(a.x) + row * W;
   const T* u = static_cast<const T*>(a.update) + row * W;
   T* ro = static_cast<T*>(a.residual_out) + row * W;
@@ -256,8 +268,8 @@ __global__ void __launch_bounds__(256) rln_scalar_kernel(const RlnArgs a) {
   const T* bp = static_cast<const T*>(a.bias);
   for (int64_t c = threadIdx.x; c < W; c += 256) {
     const float nrm = (residual(c) - mean) * rstd * ld_f32<T>(wp + c);
-    const float o = bp != nullptr ? nrm + ld_f32<T>(bp + c) : nrm;
-    no[c] = to_t<T>(zero_norm ? 0.f : o);
+    const float o = zero_norm ? 0.f : (bp != nullptr ? nrm + ld_f32<T>(bp + c) : nrm);
+    no[c] = to_t<T>(tf32 ? round_tf32(o) : o);
   }
 }
 

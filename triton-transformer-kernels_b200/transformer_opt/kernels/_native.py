@@ -28,6 +28,7 @@ DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 RLN_ZERO_INVALID_RESIDUAL = 1
 RLN_ZERO_INVALID_NORMALIZED = 2
 RLN_NO_UPDATE = 4
+RLN_ROUND_TF32 = 8
 
 STATUS_PIPELINE_TIMEOUT = 1
 STATUS_SELFTEST_TIMEOUT = 2

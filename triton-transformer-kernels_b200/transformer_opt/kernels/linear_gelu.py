@@ -8,9 +8,12 @@ loop at transformer_opt/submission.py:506-508) -- as one tcgen05 GEMM whose
 epilogue adds the bias and applies the GELU before the single store.
 
 float32 inputs multiply as TF32 (what an fp32 Linear computes with
-``torch.backends.cuda.matmul.allow_tf32``); float16 / bfloat16 round the
-biased fp32 sum to the input dtype before the GELU, as the unfused Linear's
-output tensor does. Unsupported calls raise ``ValueError``; a missing library
+``torch.backends.cuda.matmul.allow_tf32``). The tensor cores read the top 19
+bits of each operand (truncation); a TF32 cuBLAS matmul rounds to nearest, so
+callers that must match it pass operands already rounded to TF32 (the model
+rounds the weight once and has the preceding LayerNorm round x). float16 /
+bfloat16 round the biased fp32 sum to the input dtype before the GELU, as the
+unfused Linear's output tensor does. Unsupported calls raise ``ValueError``; a missing library
 raises ``RuntimeError``. No fallback.
 """
 
@@ -25,9 +28,16 @@ from transformer_opt.kernels import _native
 
 
 def linear_gelu_unsupported_reason(
-    x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: Optional[torch.Tensor],
+    *,
+    x_planned: bool = False,
 ) -> Optional[str]:
-    """Why ``fused_linear_gelu`` would reject these tensors, or None."""
+    """Why ``fused_linear_gelu`` would reject these tensors, or None.
+
+    With ``x_planned`` x stands for a fresh contiguous tensor of its shape,
+    dtype and device (its own strides and address are not checked)."""
     if x.device.type != "cuda":
         return "fused linear GELU requires CUDA tensors"
     reason = device_supported(x.device)
@@ -45,14 +55,14 @@ def linear_gelu_unsupported_reason(
         bias.shape != (weight.shape[0],) or bias.dtype != x.dtype or bias.device != x.device
     ):
         return "bias must be [out_features] with x's dtype and device"
-    if not x.is_contiguous() or not weight.is_contiguous() or (
+    if (not x_planned and not x.is_contiguous()) or not weight.is_contiguous() or (
         bias is not None and not bias.is_contiguous()
     ):
         return "fused linear GELU requires contiguous tensors"
     elem = x.element_size()
     if (x.shape[-1] * elem) % 16 or (weight.shape[0] * elem) % 16:
         return "in_features and out_features must be multiples of 16 bytes of elements"
-    for t in (x, weight, bias):
+    for t in (None if x_planned else x, weight, bias):
         if t is not None and t.data_ptr() % 16:
             return "tensors must be 16-byte aligned"
     return None

@@ -69,8 +69,15 @@ def fused_residual_layer_norm(
     *,
     zero_invalid_residual: bool = False,
     zero_invalid_normalized: bool = False,
+    round_normalized_tf32: bool = False,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Return ``(x + update, layer_norm(x + update))`` from one kernel."""
+    """Return ``(x + update, layer_norm(x + update))`` from one kernel.
+
+    ``round_normalized_tf32`` (float32 only; not in the reference's
+    signature) rounds the normalized output to the nearest TF32 value, the
+    operand rounding of a TF32 matmul, for the fused FFN projection whose
+    tensor cores read its input as stored.
+    """
     if x.shape != update.shape or x.ndim < 2:
         raise ValueError("x and update must have the same rank-two-or-higher shape")
     if update.device != x.device:
@@ -94,6 +101,10 @@ def fused_residual_layer_norm(
         flags |= _native.RLN_ZERO_INVALID_RESIDUAL
     if zero_invalid_normalized:
         flags |= _native.RLN_ZERO_INVALID_NORMALIZED
+    if round_normalized_tf32:
+        if x.dtype != torch.float32:
+            raise ValueError("TF32 rounding applies to float32 only")
+        flags |= _native.RLN_ROUND_TF32
     if x.numel():
         with torch.cuda.device(x.device):
             _native.residual_layer_norm_fwd(

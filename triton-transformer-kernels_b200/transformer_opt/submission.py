@@ -117,6 +117,9 @@ class UserOptimizedTransformer(TransformerWeights):
         # Derived, non-persistent inference data keyed by id(attention module):
         # (parameter signature, packed weight [3d, d], packed bias [3d]).
         self._packed_qkv_cache: Dict[int, Tuple[tuple, torch.Tensor, torch.Tensor]] = {}
+        # fp32 ffn_in weights rounded to TF32 for the fused FFN kernel, keyed
+        # like the packed QKV weights: (signature, rounded weight)
+        self._tf32_weight_cache: Dict[int, Tuple[tuple, torch.Tensor]] = {}
 
     # ------------------------------------------------------------ bookkeeping
     def reset_attention_backend_counts(self) -> None:
@@ -129,6 +132,7 @@ class UserOptimizedTransformer(TransformerWeights):
         state = super().__getstate__().copy()
         state.pop("_lock", None)
         state["_packed_qkv_cache"] = {}
+        state["_tf32_weight_cache"] = {}
         state["_graph"] = None
         state["_host_streams"] = {}
         return state
@@ -138,11 +142,13 @@ class UserOptimizedTransformer(TransformerWeights):
         self._lock = threading.RLock()
         self.__dict__.setdefault("ffn_backend", "auto")
         self.__dict__.setdefault("fused_linear_gelu_calls", 0)
+        self.__dict__.setdefault("_tf32_weight_cache", {})
 
     def _apply(self, fn, recurse=True):
         # device / dtype moves invalidate the packed projection weights and
         # release the captured graph (and its memory pool)
         self._packed_qkv_cache.clear()
+        self._tf32_weight_cache.clear()
         self.clear_cuda_graph()
         return super()._apply(fn, recurse=recurse)
 
@@ -169,6 +175,26 @@ class UserOptimizedTransformer(TransformerWeights):
         return tuple(
             (t.data_ptr(), t._version, t.device, t.dtype) for t in tensors if t is not None
         )
+
+    @staticmethod
+    def _params_signature(*tensors: Optional[torch.Tensor]) -> Optional[tuple]:
+        """Identity of parameters (see _qkv_signature), or None if untrackable."""
+        if any(t is not None and t.is_inference() for t in tensors):
+            return None
+        return tuple((t.data_ptr(), t._version, t.device, t.dtype) for t in tensors if t is not None)
+
+    def _tf32_weight(self, linear: nn.Linear) -> torch.Tensor:
+        """linear.weight rounded to the nearest TF32 values (ties away from
+        zero), the operand rounding of a TF32 matmul; cached per version."""
+        signature = self._params_signature(linear.weight)
+        cached = self._tf32_weight_cache.get(id(linear))
+        if signature is None or cached is None or cached[0] != signature:
+            bits = linear.weight.detach().contiguous().view(torch.int32)
+            rounded = ((bits + 0x1000) & -0x2000).view(torch.float32)
+            cached = (signature, rounded)
+            if signature is not None:
+                self._tf32_weight_cache[id(linear)] = cached
+        return cached[1]
 
     def _project_qkv(
         self, attn: SelfAttentionWeights, x: torch.Tensor
@@ -439,30 +465,45 @@ class UserOptimizedTransformer(TransformerWeights):
         *,
         zero_invalid_residual: bool = False,
         zero_invalid_normalized: bool = False,
+        round_normalized_tf32: bool = False,
     ) -> Tuple[torch.Tensor, torch.Tensor]:
         residual, normalized = fused_residual_layer_norm(
             x, update, norm.weight, norm.bias, norm.eps, valid_token_mask,
             zero_invalid_residual=zero_invalid_residual,
             zero_invalid_normalized=zero_invalid_normalized,
+            round_normalized_tf32=round_normalized_tf32,
         )
         self.fused_residual_layer_norm_calls += 1
         return residual, normalized
 
-    def _ffn_in_gelu(self, linear: nn.Linear, h: torch.Tensor) -> torch.Tensor:
-        """``F.gelu(linear(h), approximate="none")``, fused into one kernel
-        where ffn_backend allows it (reference: submission.py:506-508)."""
-        if self.ffn_backend != "torch" and (
-            h.dtype != torch.float32 or torch.backends.cuda.matmul.allow_tf32
-        ):
-            reason = linear_gelu_unsupported_reason(h, linear.weight, linear.bias)
-            if reason is None:
-                outputs = (h.numel() // h.shape[-1]) * linear.out_features
-                if self.ffn_backend == "b200" or outputs >= FUSED_FFN_MIN_OUTPUTS:
-                    self.fused_linear_gelu_calls += 1
-                    return fused_linear_gelu(h, linear.weight, linear.bias)
-            elif self.ffn_backend == "b200":
+    def _ffn_fused(self, linear: nn.Linear, h: torch.Tensor) -> bool:
+        """Whether ``gelu(linear(h))`` runs as the fused kernel for an FFN input
+        like h (the norm2 output has h's shape, dtype and device). fp32 goes
+        there only while TF32 matmuls are allowed -- the unfused fp32 Linear's
+        precision -- and then with TF32-rounded operands."""
+        if self.ffn_backend == "torch":
+            return False
+        if h.dtype == torch.float32 and not torch.backends.cuda.matmul.allow_tf32:
+            return False
+        reason = linear_gelu_unsupported_reason(h, linear.weight, linear.bias, x_planned=True)
+        if reason is not None:
+            if self.ffn_backend == "b200":
                 raise ValueError(f"ffn_backend='b200' cannot run this projection: {reason}")
-        return F.gelu(linear(h), approximate="none")
+            return False
+        outputs = (h.numel() // h.shape[-1]) * linear.out_features
+        return self.ffn_backend == "b200" or outputs >= FUSED_FFN_MIN_OUTPUTS
+
+    def _ffn_in_gelu(self, linear: nn.Linear, h: torch.Tensor, fused: bool) -> torch.Tensor:
+        """``F.gelu(linear(h), approximate="none")`` (reference:
+        submission.py:506-508), as one kernel when ``fused``. For fp32, h
+        arrives rounded to TF32 (the norm2 kernel's ROUND_TF32 flag) and the
+        weight is the cached TF32-rounded copy: the tensor cores then multiply
+        exactly the operands a TF32 cuBLAS matmul would."""
+        if not fused:
+            return F.gelu(linear(h), approximate="none")
+        weight = self._tf32_weight(linear) if h.dtype == torch.float32 else linear.weight
+        self.fused_linear_gelu_calls += 1
+        return fused_linear_gelu(h, weight, linear.bias)
 
     def _forward_fused(
         self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
@@ -473,9 +514,13 @@ class UserOptimizedTransformer(TransformerWeights):
         for index, layer in enumerate(self.layers):
             attn_out = self._attention(layer.attention, normalized, valid_token_mask, causal)
             del normalized
-            x, ffn_input = self._fused_residual_norm(x, attn_out, layer.norm2, valid_token_mask)
+            fused_ffn = self._ffn_fused(layer.ffn_in, x)
+            x, ffn_input = self._fused_residual_norm(
+                x, attn_out, layer.norm2, valid_token_mask,
+                round_normalized_tf32=fused_ffn and x.dtype == torch.float32,
+            )
             del attn_out
-            ffn_out = layer.ffn_out(self._ffn_in_gelu(layer.ffn_in, ffn_input))
+            ffn_out = layer.ffn_out(self._ffn_in_gelu(layer.ffn_in, ffn_input, fused_ffn))
             del ffn_input
             is_last = index + 1 == len(self.layers)
             next_norm = self.final_norm if is_last else self.layers[index + 1].norm1
@@ -537,7 +582,9 @@ class _ForwardGraph:
             self.fused_calls = model.fused_residual_layer_norm_calls - capture_fused
             self.ffn_calls = model.fused_linear_gelu_calls - capture_ffn
             # keep the packed weights the graph reads alive
-            self.packed = tuple(model._packed_qkv_cache.values())
+            self.packed = tuple(model._packed_qkv_cache.values()) + tuple(
+                model._tf32_weight_cache.values()
+            )
             self.done = torch.cuda.Event()
             self.done.record(current)
         finally:
