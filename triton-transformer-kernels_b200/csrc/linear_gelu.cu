@@ -24,19 +24,20 @@
 // leader CTA multiplies the pair's 256 x 256 tile, so every byte crossing L2
 // feeds twice the MMA work of a single-CTA 128 x 256 tile.
 //   warp 0      TMA producer (both CTAs): 128-byte K slices of x and weight
-//               into a 6-stage ring (128-byte swizzle, K-major -- both
+//               into a 6-stage (fp32) or 5-stage (16-bit) ring (128-byte swizzle, K-major -- both
 //               operands are row-major with K contiguous, what the MMA
 //               reads); completion is counted on the leader's barrier.
 //   warp 1      leader: MMA issuer, 256 x 256 per K step, into one of two
 //               TMEM accumulators (2 x 256 columns in each CTA), so the
 //               epilogue of tile i overlaps the main loop of tile i + 1.
 //               Both: TMEM allocation for the pair.
-//   warps 2-9   epilogue (both CTAs, own 128 rows): tcgen05.ld of the
-//               accumulator (warp w reads TMEM lane quarter w % 4; warps 2-5
-//               take columns 0-127, warps 6-9 columns 128-255), bias,
-//               rounding, GELU, then a swizzled staging tile in shared memory
-//               and a TMA store (32 rows x 128 bytes), so global memory sees
-//               whole lines instead of 16-byte pieces of 32 rows.
+//   warps 2-    epilogue (both CTAs, own 128 rows; 8 warps for fp32, 16 for
+//               16-bit): tcgen05.ld of the accumulator (warp w reads TMEM
+//               lane quarter w % 4; the warps of a quarter split the 256
+//               columns), bias, rounding, GELU, then a swizzled staging tile
+//               in shared memory and a TMA store (32 rows x 128 bytes), so
+//               global memory sees whole lines instead of 16-byte pieces of
+//               32 rows.
 // Tiles are walked in groups of kGroup row tiles: the pairs in flight share
 // a few row bands of x and a stretch of the weight matrix in L2.
 #include <cuda.h>
@@ -57,33 +58,36 @@ namespace lg {
 constexpr int BM = 128;             // rows per CTA (a pair tile has 2 * BM)
 constexpr int BN = 256;             // output features per tile (MMA N)
 constexpr int kHalfN = BN / 2;      // weight rows each CTA of the pair stages
-#ifndef B200TK_LG_STAGES
-#define B200TK_LG_STAGES 6
-#endif
-#ifndef B200TK_LG_EPI_WARPS
-#define B200TK_LG_EPI_WARPS 8
-#endif
-constexpr int kStages = B200TK_LG_STAGES;  // smem ring depth
-constexpr int kABytes = BM * 128;   // a 128-byte K slice of this CTA's x rows
+constexpr int kABytes = BM * 128;      // a 128-byte K slice of this CTA's x rows
 constexpr int kBBytes = kHalfN * 128;  // a 128-byte K slice of its weight rows
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kEpiWarps = B200TK_LG_EPI_WARPS;  // 2 or 4 per TMEM lane quarter
-constexpr int kColGroups = kEpiWarps / 4;      // column groups of a lane quarter
-constexpr int kColsPerWarp = BN / kColGroups;  // accumulator columns per epilogue warp
-constexpr int kChunks = kColsPerWarp / 32;     // 32-column TMEM loads per warp and tile
-constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr int kTmemCols = 2 * BN;  // two accumulators
 // Output staging: per epilogue warp one 32-row x 128-byte tile (128-byte
 // swizzle), stored to global memory by TMA.
 constexpr int kStagingBytes = 32 * 128;
-constexpr int kStagingOff = kStages * kStageBytes;
-constexpr int kBarOff = kStagingOff + kEpiWarps * kStagingBytes;
-constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers and slots, alignment slack
 constexpr int kGroup = 8;                         // pair row tiles per raster group
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
 constexpr uint64_t kPeerSettleNs = 200000ull;     // abort path: let issued copies land
 
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+// Per-dtype pipeline shape. fp32 (TF32 MMAs, erff GELU): 8 epilogue warps
+// and a 6-stage ring. 16-bit (twice the MMA rate per byte, a cheaper GELU):
+// 16 epilogue warps -- 4 per TMEM lane quarter hide the TMEM-load and store
+// latencies that bound the short-K shapes -- and the 5 stages that then fit.
+template <typename T>
+struct Layout {
+  static constexpr bool kWide = std::is_same_v<T, float>;  // 32 outputs per staging row
+  static constexpr int kStages = kWide ? 6 : 5;
+  static constexpr int kEpiWarps = kWide ? 8 : 16;
+  static constexpr int kColGroups = kEpiWarps / 4;      // column groups of a lane quarter
+  static constexpr int kColsPerWarp = BN / kColGroups;  // accumulator columns per warp
+  static constexpr int kChunks = kColsPerWarp / 32;     // 32-column TMEM loads per tile
+  static constexpr int kThreads = 32 * (2 + kEpiWarps);
+  static constexpr int kStagingOff = kStages * kStageBytes;
+  static constexpr int kBarOff = kStagingOff + kEpiWarps * kStagingBytes;
+  static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers and slots, alignment
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kChunks % 2 == 0, "chunks are processed in pairs");
+};
 
 struct __align__(64) LgParams {
   CUtensorMap tm_x;  // [rows, k] row-major, box {128 bytes, BM rows}
@@ -134,6 +138,31 @@ __device__ __forceinline__ float gelu_erf(float v) {
   return v * 0.5f * (1.0f + erff(v * kAlpha));
 }
 
+// GELU of a value whose output is rounded to 16 bits: 1 + erf(x) is
+// 2 - erfc(|x|) for x >= 0 and erfc(|x|) below, with erfc from Abramowitz &
+// Stegun 7.1.26, erfc(x) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-x^2),
+// t = 1 / (1 + p x), |error| <= 1.5e-7 -- far below the output's rounding
+// (bf16: 2^-9 relative, fp16: 2^-12), at about half the instructions of
+// erff. Reciprocal and exponential are the hardware approximations.
+__device__ __forceinline__ float gelu_poly(float v) {
+  const float x = fabsf(v) * 0.70710678118654752f;
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, x, 1.0f)));
+  float y = fmaf(t, 1.061405429f, -1.453152027f);
+  y = fmaf(t, y, 1.421413741f);
+  y = fmaf(t, y, -0.284496736f);
+  y = fmaf(t, y, 0.254829592f);
+  y *= t;
+  const float q = y * ex2_approx(x * x * -1.4426950408889634f);  // erfc(|v| / sqrt(2))
+  return 0.5f * v * (v >= 0.f ? 2.0f - q : q);
+}
+
+template <typename T>
+__device__ __forceinline__ float gelu_out(float v) {
+  if constexpr (std::is_same_v<T, float>) return gelu_erf(v);
+  else return gelu_poly(v);
+}
+
 // Four bias values starting at b (16-byte aligned for fp32, 8 for 16-bit).
 template <typename T>
 __device__ __forceinline__ void load_bias4(const T* b, float (&out)[4]) {
@@ -161,7 +190,13 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) linear_gelu_kernel(const __grid_constant__ LgParams p) {
+__global__ void __launch_bounds__(Layout<T>::kThreads, 1)
+    linear_gelu_kernel(const __grid_constant__ LgParams p) {
+  using L = Layout<T>;
+  constexpr int kStages = L::kStages;
+  constexpr int kEpiWarps = L::kEpiWarps;
+  constexpr int kColsPerWarp = L::kColsPerWarp;
+  constexpr int kChunks = L::kChunks;
   constexpr int kBK = 128 / static_cast<int>(sizeof(T));    // K elements per stage
   constexpr int kUmmaK = 32 / static_cast<int>(sizeof(T));  // K per MMA instruction
   constexpr int kSteps = kBK / kUmmaK;                       // MMAs per stage (4)
@@ -173,14 +208,14 @@ __global__ void __launch_bounds__(kThreads, 1) linear_gelu_kernel(const __grid_c
   // acc_empty[b] are used in the leader only (the peer's producer and
   // epilogue signal the leader's); empty[s] and acc_full[b] exist in both
   // and are signalled by the leader's MMA commits (multicast to the pair).
-  const uint32_t bar0 = sbase + kBarOff;
+  const uint32_t bar0 = sbase + L::kBarOff;
   auto bar_full = [&](int s) { return bar0 + 8 * s; };
   auto bar_empty = [&](int s) { return bar0 + 8 * (kStages + s); };
   auto bar_acc_full = [&](int b) { return bar0 + 8 * (2 * kStages + b); };
   auto bar_acc_empty = [&](int b) { return bar0 + 8 * (2 * kStages + 2 + b); };
   const uint32_t bar_drain = bar0 + 8 * (2 * kStages + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBarOff + 192);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + 200);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBarOff + 192);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kBarOff + 200);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -358,9 +393,9 @@ __global__ void __launch_bounds__(kThreads, 1) linear_gelu_kernel(const __grid_c
     const int row = quarter * 32 + lane;  // CTA tile row == TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t acc_empty_leader = mapa_shared(bar_acc_empty(0), 0);
-    const uint32_t staging = sbase + kStagingOff + (warp - 2) * kStagingBytes;
+    const uint32_t staging = sbase + L::kStagingOff + (warp - 2) * kStagingBytes;
     const uint32_t srow = staging + lane * 128;  // this lane's staging row
-    constexpr bool kWide = std::is_same_v<T, float>;  // 32 outputs fill a staging row
+    constexpr bool kWide = L::kWide;  // 32 outputs fill a staging row
     const T* bias = static_cast<const T*>(p.bias);
     if (lane == 0) tma_prefetch_desc(&p.tm_out);
     int tc = 0;
@@ -389,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_gelu_kernel(const __grid_c
           for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xFFFFFFFFu, bl[j & 3], c * 8 + (j >> 2));
         }
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(round_to<T>(v[j]));
+        for (int j = 0; j < 32; ++j) v[j] = gelu_out<T>(round_to<T>(v[j]));
         // the staging tile is free once the previous store has read it
         if (kWide || (c & 1) == 0) {
           if (lane == 0) bulk_wait_read_all();
@@ -479,7 +514,8 @@ cudaError_t prepare(int device, int* pairs) {
   int v = cached[device].load(std::memory_order_acquire);
   if (v == 0) {
     cudaError_t err =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Layout<T>::kSmemBytes);
     if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -488,8 +524,8 @@ cudaError_t prepare(int device, int* pairs) {
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.blockDim = dim3(Layout<T>::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Layout<T>::kSmemBytes;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
@@ -517,8 +553,8 @@ cudaError_t launch_typed(const LgParams& prm, int device, cudaStream_t stream) {
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.blockDim = dim3(Layout<T>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Layout<T>::kSmemBytes;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
