@@ -597,6 +597,47 @@ def run_b200_arm(args) -> int:
     return 0
 
 
+def run_ffn_only(args) -> int:
+    """Kernel-only timing of the fused FFN input projection + GELU at the
+    configuration's shape (rows = batch x seq, d_model -> ffn), for profiling:
+    W warm-up launches, then K launches timed with CUDA events (L2 flushed
+    before each). Prints one JSON line; not the bench contract's line."""
+    from transformer_opt.kernels import fused_linear_gelu
+
+    name = args.config
+    b, s, d, h, f, layers, causal, dt = CONFIGS[name]
+    dtype = DTYPES[dt]
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device).manual_seed(0)
+    rows = b * s
+    x = torch.randn(rows, d, device=device, generator=gen).to(dtype)
+    bound = d ** -0.5  # nn.Linear's default init range
+    w = ((torch.rand(f, d, device=device, generator=gen) * 2 - 1) * bound).to(dtype)
+    bias = ((torch.rand(f, device=device, generator=gen) * 2 - 1) * bound).to(dtype)
+    out = torch.empty(rows, f, device=device, dtype=dtype)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    for _ in range(args.warmup):
+        fused_linear_gelu(x, w, bias, out=out)
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        fused_linear_gelu(x, w, bias, out=out)
+        end.record()
+        end.synchronize()
+        times.append(start.elapsed_time(end))
+    ms = statistics.median(times)
+    flops = 2.0 * rows * d * f
+    print(json.dumps({
+        "kernel": "linear_gelu_kernel", "config": describe(name), "rows": rows,
+        "in_features": d, "out_features": f, "dtype": DTYPE_TAG[dt], "ms": ms,
+        "tflops": flops / (ms / 1000.0) / 1e12, "launches": args.warmup + args.steps,
+    }), flush=True)
+    return 0
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -612,6 +653,8 @@ def main() -> int:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--ref-budget", type=float, default=15.0,
                         help="seconds of CPU work per reference sample")
+    parser.add_argument("--ffn-only", action="store_true",
+                        help="time only the fused FFN projection kernel (profiling)")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         parser.error("--warmup must be >= 3")
@@ -621,6 +664,8 @@ def main() -> int:
         CONFIGS[args.config] = (args.batch,) + tuple(CONFIGS[args.config][1:])
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.ffn_only:
+        return run_ffn_only(args)
     return run_b200_arm(args)
 
 
