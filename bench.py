@@ -480,6 +480,7 @@ def run_b200_arm(args) -> int:
         barrier(world)
         torch.cuda.synchronize(device)
         e2e_chunks = model.default_host_plan(b, s)  # sequences per chunk
+        e2e_replays_before = model.cuda_graph_replays
         for _ in range(args.warmup):  # per-stream allocator pools, as in the device region
             model.forward_host(x_host, out=y_host, chunks=e2e_chunks)
         torch.cuda.synchronize(device)
@@ -495,6 +496,7 @@ def run_b200_arm(args) -> int:
             model.forward_host(x_host, out=y_host, chunks=e2e_chunks, synchronize=False)
             e_ends[i].record(stream)
         torch.cuda.synchronize(device)
+        e2e_graphed = model.cuda_graph_replays > e2e_replays_before
         y = y_host.to(device)  # the host-API result is the one validated
         barrier(world)
         e2e_local = sum(a.elapsed_time(b_) for a, b_ in zip(e_starts, e_ends)) / args.steps
@@ -562,6 +564,7 @@ def run_b200_arm(args) -> int:
             "d2h_bytes_per_step": x.numel() * x.element_size(),
             "api": "UserOptimizedTransformer.forward_host (pinned host buffers)",
             "chunks": e2e_chunks,
+            "chunk_forwards": "CUDA-graph replay" if e2e_graphed else "eager",
         },
         "roofline": roofline,
         "rln": {

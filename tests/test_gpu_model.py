@@ -322,3 +322,28 @@ def test_forward_host_without_synchronize_is_ordered_on_the_current_stream():
                 assert torch.equal(out, ref)
             else:  # other GEMM shapes: equal within the harness rule
                 assert _harness_close(out, ref)
+
+
+def test_forward_host_replays_captured_chunk_forwards_unless_eager():
+    torch.manual_seed(6)
+    shape = TransformerConfig(8, 256, 256, 4, 1024, 2, True)
+    auto = UserOptimizedTransformer(shape).to("cuda").eval()
+    eager = UserOptimizedTransformer(shape, execution_mode="eager").to("cuda").eval()
+    eager.load_state_dict(auto.state_dict())
+    x_host = torch.randn(8, 256, 256).pin_memory()
+    with torch.inference_mode():
+        for plan in ([2, 2, 2, 2], [1, 3, 2, 2], [2, 2, 2, 2]):
+            y = auto.forward_host(x_host, chunks=plan)
+            ref = eager.forward_host(x_host, chunks=plan)
+            assert torch.equal(y, ref)  # same kernels in the same order
+    # one replay per chunk; captures for sizes 2, 1 and 3, kept for reuse
+    assert auto.cuda_graph_replays == 12
+    assert eager.cuda_graph_replays == 0
+    assert len(auto._graphs) == 3
+    # a parameter update makes every capture stale: the next miss drops them
+    with torch.no_grad():
+        auto.layers[0].ffn_out.bias.add_(0.5)
+        eager.layers[0].ffn_out.bias.add_(0.5)
+    with torch.inference_mode():
+        assert torch.equal(auto.forward_host(x_host, chunks=4), eager.forward_host(x_host, chunks=4))
+    assert len(auto._graphs) == 1

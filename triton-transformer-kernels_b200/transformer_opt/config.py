@@ -63,13 +63,22 @@ def _validate_qkv_contract(
     return None
 
 
+# Compute capability per CUDA device index (a device's capability never
+# changes; the model asks on every layer, so the query is made once).
+_CAPABILITY: dict = {}
+
+
 def device_supported(device: torch.device) -> Optional[str]:
     """None when `device` can run the sm_100a kernels, else the reason."""
     if device.type != "cuda":
         return "custom attention requires CUDA tensors"
     if not torch.cuda.is_available():
         return "CUDA is unavailable"
-    capability = torch.cuda.get_device_capability(device)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    capability = _CAPABILITY.get(index)
+    if capability is None:
+        capability = torch.cuda.get_device_capability(index)
+        _CAPABILITY[index] = capability
     if capability < MIN_CUDA_CAPABILITY or capability > MAX_CUDA_CAPABILITY:
         return (
             f"compute capability {capability} is not sm_100 "

@@ -10,7 +10,8 @@ execution_mode: "eager" launches the fused forward op by op; "graph" captures
 it once per input signature into a CUDA graph and replays it (fresh input
 copied into the graph's static buffer, output cloned so results never alias,
 the reference's _InferenceGraph contract, submission.py:674-723); "auto"
-replays only launch-bound forwards (AUTO_GRAPH_MAX_ELEMENTS).
+replays only launch-bound forwards (AUTO_GRAPH_MAX_ELEMENTS) and the chunk
+forwards of forward_host. Up to GRAPH_CACHE_SIZE captures are kept.
 
 On an sm_100 GPU in inference mode every layer runs
   packed QKV projection (cuBLAS, fp32) or three projections (16-bit)
@@ -32,6 +33,7 @@ PyTorch forward with attention through ``attention_forward``.
 from __future__ import annotations
 
 import threading
+from collections import OrderedDict
 from typing import Dict, List, Optional, Sequence, Tuple, Union
 
 import torch
@@ -75,6 +77,10 @@ AUTO_GRAPH_MAX_ELEMENTS = 1 << 22
 HOST_MIN_CHUNK_TOKENS = 4096
 HOST_MAX_CHUNKS = 8
 HOST_STREAMS = 3
+# Captured forwards kept per model (one per input signature, least recently
+# used dropped first): forward_host's plans have at most two chunk sizes, and
+# a caller may alternate them with a whole-batch forward.
+GRAPH_CACHE_SIZE = 4
 
 __all__ = ["TransformerConfig", "UserOptimizedTransformer"]
 
@@ -112,7 +118,7 @@ class UserOptimizedTransformer(TransformerWeights):
         self.fused_residual_layer_norm_calls = 0
         self.fused_linear_gelu_calls = 0
         self.cuda_graph_replays = 0
-        self._graph: Optional["_ForwardGraph"] = None
+        self._graphs: "OrderedDict[tuple, _ForwardGraph]" = OrderedDict()
         self._host_streams: Dict[int, Tuple[torch.cuda.Stream, ...]] = {}
         # Derived, non-persistent inference data keyed by id(attention module):
         # (parameter signature, packed weight [3d, d], packed bias [3d]).
@@ -133,7 +139,7 @@ class UserOptimizedTransformer(TransformerWeights):
         state.pop("_lock", None)
         state["_packed_qkv_cache"] = {}
         state["_tf32_weight_cache"] = {}
-        state["_graph"] = None
+        state["_graphs"] = OrderedDict()
         state["_host_streams"] = {}
         return state
 
@@ -143,6 +149,7 @@ class UserOptimizedTransformer(TransformerWeights):
         self.__dict__.setdefault("ffn_backend", "auto")
         self.__dict__.setdefault("fused_linear_gelu_calls", 0)
         self.__dict__.setdefault("_tf32_weight_cache", {})
+        self.__dict__.setdefault("_graphs", OrderedDict())
 
     def _apply(self, fn, recurse=True):
         # device / dtype moves invalidate the packed projection weights and
@@ -153,9 +160,9 @@ class UserOptimizedTransformer(TransformerWeights):
         return super()._apply(fn, recurse=recurse)
 
     def clear_cuda_graph(self) -> None:
-        """Release the cached capture; a later eligible call captures again."""
+        """Release the cached captures; a later eligible call captures again."""
         with self._lock:
-            self._graph = None
+            self._graphs.clear()
 
     # ------------------------------------------------------------ projections
     @staticmethod
@@ -294,7 +301,10 @@ class UserOptimizedTransformer(TransformerWeights):
         sequence summing to the batch), or by default ``default_host_plan``.
         Each group's host-to-device copy, forward and device-to-host copy run in
         order on one of HOST_STREAMS CUDA streams, so the transfers of one
-        group overlap the compute of the others. Sequences do not interact
+        group overlap the compute of the others. Unless execution_mode is
+        "eager", each group's forward replays a captured CUDA graph (one per
+        group size): a group's eager forward costs more host time than GPU
+        time. Sequences do not interact
         in this model: the result is the forward of each group. Pinned host
         memory makes the copies asynchronous (pageable memory works, with
         synchronous copies). The call returns once ``out`` holds the result;
@@ -338,6 +348,11 @@ class UserOptimizedTransformer(TransformerWeights):
                 current.synchronize()
             return out
         streams = self._streams_for(device)
+        # A chunk's forward is launch-bound on the host (measured on C2: ~1.4 ms
+        # of Python and launch work per 2-sequence chunk, more than its GPU
+        # time), so unless the model is "eager" each chunk replays a captured
+        # forward; equal chunks share one capture.
+        replay = self.execution_mode != "eager"
         done = []
         start = 0
         for i, size in enumerate(sizes):
@@ -350,7 +365,7 @@ class UserOptimizedTransformer(TransformerWeights):
                 ms = None
                 if valid_token_mask is not None:
                     ms = valid_token_mask[rows].to(device, non_blocking=True)
-                out[rows].copy_(self.forward(xs, ms), non_blocking=True)
+                out[rows].copy_(self._chunk_forward(xs, ms, replay), non_blocking=True)
                 event = torch.cuda.Event()
                 event.record(stream)
                 done.append(event)
@@ -360,6 +375,17 @@ class UserOptimizedTransformer(TransformerWeights):
             for event in done:
                 event.synchronize()
         return out
+
+    def _chunk_forward(self, x, valid_token_mask, replay: bool) -> torch.Tensor:
+        """forward() of one forward_host chunk, replayed from a capture when
+        ``replay`` and the fused route apply (whatever the chunk's size)."""
+        if replay and self.fused_route_reason(x, valid_token_mask) is None:
+            if not torch.cuda.is_current_stream_capturing():
+                _native.load()
+                signature = self._graph_signature(x, valid_token_mask)
+                if signature is not None:
+                    return self._graph_forward(x, valid_token_mask, signature)
+        return self.forward(x, valid_token_mask)
 
     @staticmethod
     def default_host_chunks(batch: int, seq: int) -> int:
@@ -442,11 +468,18 @@ class UserOptimizedTransformer(TransformerWeights):
 
     def _graph_forward(self, x, valid_token_mask, signature) -> torch.Tensor:
         with self._lock:
-            graph = self._graph
-            if graph is None or graph.signature != signature:
-                self._graph = None
+            graph = self._graphs.get(signature)
+            if graph is None:
+                # captures made with other parameters (or parameter versions)
+                # can never replay again: release them first
+                for key in [k for k in self._graphs if k[0] != signature[0]]:
+                    del self._graphs[key]
+                while len(self._graphs) >= GRAPH_CACHE_SIZE:
+                    self._graphs.popitem(last=False)
                 graph = _ForwardGraph(self, x, valid_token_mask, signature)
-                self._graph = graph
+                self._graphs[signature] = graph
+            else:
+                self._graphs.move_to_end(signature)
             out = graph.replay(x, valid_token_mask)
             for backend, count in graph.backend_counts.items():
                 self.attention_backend_counts[backend] += count
