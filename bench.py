@@ -479,7 +479,7 @@ def run_b200_arm(args) -> int:
         e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier(world)
         torch.cuda.synchronize(device)
-        e2e_chunks = model.default_host_plan(b, s)  # sequences per chunk
+        e2e_chunks = model.default_host_plan(b, s, d)  # sequences per chunk
         e2e_replays_before = model.cuda_graph_replays
         for _ in range(args.warmup):  # per-stream allocator pools, as in the device region
             model.forward_host(x_host, out=y_host, chunks=e2e_chunks)

@@ -136,20 +136,24 @@ def test_forward_host_on_a_cpu_model_is_forward():
         assert model.forward_host(x, out=out) is out and torch.equal(out, ref)
 
 
-def test_default_host_chunks_keep_whole_sequences_and_enough_tokens():
+def test_default_host_chunks_keep_whole_sequences_and_enough_elements():
     chunks = UserOptimizedTransformer.default_host_chunks
-    assert chunks(8, 2048) == 4      # 2 sequences (4096 tokens) per chunk
+    assert chunks(8, 2048) == 4      # 2 sequences (4096 tokens x 1024) per chunk
     assert chunks(512, 512) == 8     # capped at 8 chunks
     assert chunks(4, 16384) == 4     # one sequence per chunk
-    assert chunks(4, 512) == 1       # too few tokens to split
+    assert chunks(4, 512) == 1       # too few elements to split at width 1024
+    assert chunks(4, 512, 4096) == 2  # ... but enough at d_model 4096 (C4)
     assert chunks(7, 4096) == 7      # divisors of the batch only
     assert chunks(7, 2048) == 1
     assert chunks(1, 1) == 1
     plan = UserOptimizedTransformer.default_host_plan
-    assert plan(8, 2048) == [2, 2, 2, 2]                  # halves would hold 2048 tokens
-    assert plan(512, 512) == [32] + [64] * 7 + [32]       # first and last chunks halved
-    assert plan(4, 16384) == [1, 1, 1, 1]
-    assert sum(plan(512, 512)) == 512
+    assert plan(8, 2048, 1024) == [1, 2, 2, 2, 1]          # C2: halves keep 2048 x 1024
+    assert plan(512, 512, 768) == [32] + [64] * 7 + [32]   # C5
+    assert plan(4, 16384, 4096) == [1, 1, 1, 1]            # C3: a sequence cannot be halved
+    assert plan(4, 512, 4096) == [1, 2, 1]                 # C4
+    assert plan(2, 128, 256) == [2]                        # C1: one chunk
+    assert plan(8, 1024, 1024) == [2, 4, 2]                # 4-sequence chunks, halved ends
+    assert sum(plan(512, 512, 768)) == 512
 
 
 def test_forward_host_accepts_chunk_sizes_on_a_cpu_model():
