@@ -168,11 +168,14 @@ def test_c3_bf16_model_rows_error_budget_parity():
     assert optimized.attention_backend_counts["b200"] == 2
 
 
+@pytest.mark.parametrize("ffn_backend", ["auto", "b200"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("causal", [False, True])
-def test_padded_batches_match_explicit_baseline(dtype, causal):
+def test_padded_batches_match_explicit_baseline(dtype, causal, ffn_backend):
+    # "auto" keeps this small FFN projection on cuBLAS; "b200" forces the
+    # fused kernel (fp32: with TF32-rounded operands) on ragged row tiles
     shape = (3, 200, 256, 4, 512, 2, causal)
-    baseline, optimized = build_pair(shape, dtype)
+    baseline, optimized = build_pair(shape, dtype, ffn_backend=ffn_backend)
     cfg = oracle.TransformerConfig(*shape)
     truth = truth_model(baseline) if dtype == torch.bfloat16 else None
     for seed in range(3):
@@ -188,6 +191,7 @@ def test_padded_batches_match_explicit_baseline(dtype, causal):
                 res = oracle.compare_outputs(ref, out)
                 assert res.passed, res
         assert torch.count_nonzero(out[~mask]) == 0
+    assert optimized.fused_linear_gelu_calls == (3 * 2 if ffn_backend == "b200" else 0)
 
 
 def test_small_head_dims_run_the_generic_kernel_inside_the_model():
