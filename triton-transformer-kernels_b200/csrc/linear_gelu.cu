@@ -94,7 +94,6 @@ struct __align__(64) LgParams {
   CUtensorMap tm_w;  // [n, k] row-major, box {128 bytes, kHalfN rows}
   CUtensorMap tm_out;  // [rows, n] row-major, box {128 bytes, 32 rows}
   const void* bias;  // [n] or nullptr
-  void* out;         // [rows, n] row-major
   int64_t rows;
   int n_out;
   int m_tiles, n_tiles, k_blocks;
@@ -571,7 +570,6 @@ cudaError_t launch_linear_gelu(const LinearGeluArgs& a, cudaStream_t stream) {
   prm.tm_w = *reinterpret_cast<const CUtensorMap*>(a.tm_w);
   prm.tm_out = *reinterpret_cast<const CUtensorMap*>(a.tm_out);
   prm.bias = a.bias;
-  prm.out = a.out;
   prm.rows = a.rows;
   prm.n_out = static_cast<int>(a.n_out);
   const int es = a.dtype == B200TK_DTYPE_FLOAT32 ? 4 : 2;

@@ -1,6 +1,8 @@
 // ptx_sm100.cuh - thin inline-PTX wrappers for the sm_100a features the
-// kernels use: mbarriers with bounded waits, TMA tensor loads, and the
-// tcgen05 family (TMEM allocation, MMA, loads/stores, fences, commits).
+// kernels use: mbarriers with bounded waits, TMA tensor loads and stores,
+// CTA-pair (cluster) addressing and synchronisation, and the tcgen05 family
+// (TMEM allocation, MMA in single-CTA and pair forms, loads/stores, fences,
+// commits).
 #pragma once
 
 #include <cstdint>
@@ -92,17 +94,6 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(desc)) : "memory");
-}
-
-// 2D tiled load (no multicast). c0 (innermost, elements) is always a
-// multiple of 16 bytes here.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* desc, uint32_t bar, int c0,
-                                            int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(c0), "r"(c1)
-      : "memory");
 }
 
 // 2D tiled store from this CTA's shared memory (bulk-group completion). c0
