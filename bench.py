@@ -58,6 +58,15 @@ NCU_ATTENTION_TRAFFIC = {
     # + 113.8 MB written), scaled by C3's 4 independent sequences
     "C3": 4 * 537.7e6,
 }
+# DRAM bytes per launch of the fused FFN projection, same method.
+NCU_FFN_TRAFFIC = {
+    # profiles/linear_gelu_tf32_C2.md: 113.0 MB read + 218.4 MB written
+    "C2": 331.4e6,
+    # profiles/linear_gelu_bf16_C5.md: captured on a quarter of C5's rows
+    # (105.6 MB read + 344.8 MB written), scaled by 4 (rows are independent;
+    # x and the output scale with rows, the 4.7 MB weight is re-read per band)
+    "C5": 4 * 450.4e6,
+}
 
 
 def describe(name: str) -> str:
@@ -167,7 +176,7 @@ class ClockSampler:
         }
 
 
-def ffn_summary(ms, flops, launches_per_step, dtype, peaks):
+def ffn_summary(ms, flops, launches_per_step, dtype, peaks, traffic=None):
     """Roofline of the fused FFN input projection + GELU (one GEMM per layer)."""
     if launches_per_step == 0:
         return {"fused": False}
@@ -187,6 +196,7 @@ def ffn_summary(ms, flops, launches_per_step, dtype, peaks):
         "frac": achieved / peak,
         "peak_source": f"{peaks['source']} bf16_tflops_sustained"
         + (" / 2 (TF32)" if dtype == torch.float32 else ""),
+        "traffic": traffic,
     }
 
 
@@ -576,7 +586,10 @@ def run_b200_arm(args) -> int:
             "launch_ms": rln_ms,
             "bytes_per_launch": rln_bytes,
         },
-        "ffn_in_gelu": ffn_summary(ffn_ms, ffn_flops, ffn_launches, dtype, peaks),
+        "ffn_in_gelu": ffn_summary(
+            ffn_ms, ffn_flops, ffn_launches, dtype, peaks,
+            NCU_FFN_TRAFFIC.get(name) if args.batch is None else None,
+        ),
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "validation": {
