@@ -351,3 +351,23 @@ def test_forward_host_replays_captured_chunk_forwards_unless_eager():
     with torch.inference_mode():
         assert torch.equal(auto.forward_host(x_host, chunks=4), eager.forward_host(x_host, chunks=4))
     assert len(auto._graphs) == 1
+
+
+def test_graph_cache_keeps_the_most_recent_captures():
+    from transformer_opt.submission import GRAPH_CACHE_SIZE
+
+    torch.manual_seed(9)
+    graph = _graph_pair("graph")
+    eager = _graph_pair("eager")
+    eager.load_state_dict(graph.state_dict())
+    xs = {n: torch.randn(n, 128, 256, device="cuda") for n in range(1, GRAPH_CACHE_SIZE + 3)}
+    with torch.inference_mode():
+        for n, x in xs.items():  # one capture per batch size, oldest evicted
+            assert torch.equal(graph(x), eager(x))
+        assert len(graph._graphs) == GRAPH_CACHE_SIZE
+        kept = [key[5][0] for key in graph._graphs]  # batch size of each kept capture
+        assert kept == list(xs)[-GRAPH_CACHE_SIZE:]
+        n_first = next(iter(xs))
+        assert torch.equal(graph(xs[n_first]), eager(xs[n_first]))  # recaptured
+        assert len(graph._graphs) == GRAPH_CACHE_SIZE
+    assert graph.cuda_graph_replays == len(xs) + 1
