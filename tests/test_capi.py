@@ -119,3 +119,17 @@ def test_linear_gelu_validation_errors_need_no_gpu():
     assert lib.b200tk_linear_gelu_fwd(odd, p, None, p, 0, 4, 64, 64, None) == _native.ERR_UNSUPPORTED
     # zero rows: nothing to launch
     assert lib.b200tk_linear_gelu_fwd(p, p, None, p, 0, 0, 64, 64, None) == _native.OK
+
+
+def test_residual_layer_norm_round_tf32_flag_validation_needs_no_gpu():
+    lib = _native.load()
+    p = ctypes.c_void_p(16)
+    flag = _native.RLN_ROUND_TF32
+    # TF32 rounding of the normalized output is defined for float32 only
+    rc = lib.b200tk_residual_layer_norm_fwd(p, p, p, None, None, p, p, 2, 4, 64, 1e-5, flag, None)
+    assert rc == _native.ERR_INVALID_ARGUMENT
+    assert b"float32" in lib.b200tk_last_error()
+    rc = lib.b200tk_residual_layer_norm_fwd(p, p, p, None, None, p, p, 0, 4, 64, 1e-5, 16, None)
+    assert rc == _native.ERR_INVALID_ARGUMENT  # unknown flag bit
+    rc = lib.b200tk_residual_layer_norm_fwd(p, p, p, None, None, p, p, 0, 0, 64, 1e-5, flag, None)
+    assert rc == _native.OK  # float32 with the flag, zero rows: nothing to launch
