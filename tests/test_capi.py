@@ -48,6 +48,7 @@ def test_header_constants_match_binding():
     assert const("B200TK_DTYPE_FLOAT16") == _native.DTYPE_CODES[torch.float16]
     assert const("B200TK_DTYPE_BFLOAT16") == _native.DTYPE_CODES[torch.bfloat16]
     assert const("B200TK_RLN_NO_UPDATE") == _native.RLN_NO_UPDATE
+    assert const("B200TK_RLN_ROUND_TF32") == _native.RLN_ROUND_TF32
     assert const("B200TK_ROUTE_TCGEN05") == _native.ROUTE_TCGEN05
 
 
