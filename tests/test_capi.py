@@ -134,3 +134,21 @@ def test_residual_layer_norm_round_tf32_flag_validation_needs_no_gpu():
     assert rc == _native.ERR_INVALID_ARGUMENT  # unknown flag bit
     rc = lib.b200tk_residual_layer_norm_fwd(p, p, p, None, None, p, p, 0, 0, 64, 1e-5, flag, None)
     assert rc == _native.OK  # float32 with the flag, zero rows: nothing to launch
+
+
+def test_work_item_range_is_checked_before_any_launch():
+    # bf16 head_dim 128: 256 query rows per item. S = 768 gives 3 tiles per
+    # (batch, head); the causal pair schedule numbers 4 items per batch-head,
+    # and 4 * 2^29 items overflow int while 3 * 2^29 do not: the shape must be
+    # rejected by the host-side check, not launched with a wrapped count.
+    s, h, d = 768, 512, 128
+    contiguous = (s * h * d, h * d, d)
+    base = 1 << 20
+    ptrs = (base, base, base)
+    assert _route(ptrs, [contiguous] * 3, shape=(1 << 20, s, h, d)) == _native.ERR_UNSUPPORTED
+    assert b"work-item" in _native.load().b200tk_last_error()
+    assert _route(ptrs, [contiguous] * 3, shape=(1 << 10, s, h, d)) == _native.ROUTE_TCGEN05
+    # the CUDA-core route (head_dim 32: 128 rows per CTA, 6 per batch-head)
+    narrow = (s * h * 32, h * 32, 32)
+    assert _route(ptrs, [narrow] * 3, shape=(1 << 20, s, h, 32)) == _native.ERR_UNSUPPORTED
+    assert _route(ptrs, [narrow] * 3, shape=(1 << 10, s, h, 32)) == _native.ROUTE_GENERIC

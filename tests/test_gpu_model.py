@@ -4,23 +4,23 @@ The harness contract (benchmarks/torch_transformer_benchmark.py:666-743 of
 the reference): both models get identical weights through a strict state-dict
 copy, run on the GPU under the same precision flags (TF32 matmuls allowed,
 float32 matmul precision "high"), and every output element must satisfy
-abs_err <= 1e-3 OR abs_err <= 1e-2 * |ref| (:309-316), on 5 seeds. float32
-and float16 models are held to exactly that rule.
+abs_err <= 1e-3 OR abs_err <= 1e-2 * |ref| (:309-316), on 5 seeds.
 
-bfloat16 models are held to error-budget parity instead: the same weights run
-in float32 with full-precision matmuls give the "truth", and the fused model's
-deviation from the truth (mean and the fraction of elements outside the rule)
-must not exceed the explicit bf16 baseline's own deviation by more than 5%.
-The element-wise rule against the bf16 baseline cannot hold for a deep bf16
-stack unless every op reproduces the baseline's reduction order bit for bit:
-the baseline itself misses the rule against the truth on ~40% of C5's
-elements, and swapping a single op (attention or LayerNorm alone) for a
-correctly rounded equivalent already moves ~32% of C5's outputs outside it.
-The attention kernel itself passes the element-wise rule in
-tests/test_gpu_attention.py.
-
-C3 (S = 16384) is checked on a subset of rows with the oracle's row-restricted
-forward (exact for its single layer).
+* float32 / float16 models (C1, C2, C4, padded cases): that rule on every
+  output element.
+* C3 (bfloat16, one layer, S = 16384): that rule on every output element of
+  the full explicit model, run one batch element at a time (its scores do not
+  fit otherwise); the fused model runs the same slices so both sides issue
+  the same GEMM shapes.
+* C5 (bfloat16, 12 layers): that rule per layer -- every fused block is fed
+  the explicit model's own input to that block and its output residual
+  stream (and, after the last block, the final LayerNorm) is compared with
+  the explicit block's. Across the whole 12-layer stack the rule cannot hold
+  for bfloat16 unless every op reproduces the baseline's reduction order bit
+  for bit (the baseline itself misses it against an fp32 truth on ~40% of
+  C5's elements), so the whole stack is held to error-budget parity: no
+  further from an fp32 truth (same weights, full-precision matmuls) than the
+  explicit bf16 model, mean error and rule-failure fraction within 5%.
 """
 
 from __future__ import annotations
@@ -142,6 +142,9 @@ def test_c5_bf16_model_error_budget_parity_on_five_seeds():
             with full_fp32_matmuls():
                 exact = truth(x.float(), mask)
         stats = assert_error_budget_parity(exact, ref, out)
+        # reported, not asserted: the element-wise rule against the explicit
+        # bf16 stack itself (see the module docstring)
+        stats["rule_fail_vs_explicit"] = _rule_fail_fraction(ref, out)[0]
         print(f"C5 seed {seed}: {stats}")
         del ref, out, exact
     assert optimized.attention_backend_counts["b200"] == 5 * shape[5]
@@ -149,23 +152,54 @@ def test_c5_bf16_model_error_budget_parity_on_five_seeds():
     assert _native.device_status(0) == 0
 
 
-def test_c3_bf16_model_rows_error_budget_parity():
-    shape, dtype = CONFIGS["C3"]
+def test_c5_bf16_every_layer_matches_the_explicit_block_on_five_seeds():
+    shape, dtype = CONFIGS["C5"]
     baseline, optimized = build_pair(shape, dtype)
-    truth = truth_model(baseline)
     cfg = oracle.TransformerConfig(*shape)
-    s = shape[1]
-    rows = [0, 1, 255, 4096, 8191, 12345, s - 129, s - 1]
-    for seed in range(2):
+    layers = shape[5]
+    failures = []
+    for seed in range(5):
         x, mask = oracle.generate_random_case(cfg, torch.device("cuda"), dtype, seed)
         with torch.inference_mode():
-            out = optimized(x, mask)[:, rows]
-            ref = oracle.baseline_forward_rows(baseline, x, rows, mask)
-            with full_fp32_matmuls():
-                exact = oracle.baseline_forward_rows(truth, x.float(), rows, mask)
-        stats = assert_error_budget_parity(exact, ref, out)
-        print(f"C3 seed {seed}: {stats}")
-    assert optimized.attention_backend_counts["b200"] == 2
+            for i in range(layers):
+                expected = baseline.layers[i](x, mask, cfg.causal)
+                residual, normalized = optimized.forward_layer(i, x, mask)
+                res = oracle.compare_outputs(expected, residual)
+                if not res.passed:
+                    failures.append((seed, i, "block", res))
+                if i == layers - 1:
+                    final = oracle.compare_outputs(baseline.final_norm(expected), normalized)
+                    if not final.passed:
+                        failures.append((seed, i, "final_norm", final))
+                x = expected  # the next block gets the explicit model's input
+                del residual, normalized
+    assert optimized.attention_backend_counts["b200"] == 5 * layers
+    assert optimized.fused_linear_gelu_calls == 5 * layers
+    assert not failures, failures
+    assert _native.device_status(0) == 0
+
+
+def test_c3_bf16_model_matches_the_explicit_model_on_five_seeds():
+    shape, dtype = CONFIGS["C3"]
+    baseline, optimized = build_pair(shape, dtype)
+    cfg = oracle.TransformerConfig(*shape)
+    failures = []
+    for seed in range(5):
+        x, mask = oracle.generate_random_case(cfg, torch.device("cuda"), dtype, seed)
+        for b in range(shape[0]):
+            with torch.inference_mode():
+                ref = baseline(x[b : b + 1])
+                out = optimized(x[b : b + 1])
+                res = oracle.compare_outputs(ref, out)
+            print(f"C3 seed {seed} batch {b}: failed {res.failed_elements} of "
+                  f"{res.total_elements}, max abs {res.max_abs_error:.3g}")
+            if not res.passed:
+                failures.append((seed, b, res))
+            del ref, out
+            torch.cuda.empty_cache()
+    assert optimized.attention_backend_counts["b200"] == 5 * shape[0]
+    assert not failures, failures
+    assert _native.device_status(0) == 0
 
 
 @pytest.mark.parametrize("ffn_backend", ["auto", "b200"])
@@ -343,14 +377,14 @@ def test_forward_host_replays_captured_chunk_forwards_unless_eager():
     # one replay per chunk; captures for sizes 2, 1 and 3, kept for reuse
     assert auto.cuda_graph_replays == 12
     assert eager.cuda_graph_replays == 0
-    assert len(auto._graphs) == 3
+    assert len(auto._captures) == 3
     # a parameter update makes every capture stale: the next miss drops them
     with torch.no_grad():
         auto.layers[0].ffn_out.bias.add_(0.5)
         eager.layers[0].ffn_out.bias.add_(0.5)
     with torch.inference_mode():
         assert torch.equal(auto.forward_host(x_host, chunks=4), eager.forward_host(x_host, chunks=4))
-    assert len(auto._graphs) == 1
+    assert len(auto._captures) == 1
 
 
 def test_graph_cache_keeps_the_most_recent_captures():
@@ -364,10 +398,56 @@ def test_graph_cache_keeps_the_most_recent_captures():
     with torch.inference_mode():
         for n, x in xs.items():  # one capture per batch size, oldest evicted
             assert torch.equal(graph(x), eager(x))
-        assert len(graph._graphs) == GRAPH_CACHE_SIZE
-        kept = [key[5][0] for key in graph._graphs]  # batch size of each kept capture
+        assert len(graph._captures) == GRAPH_CACHE_SIZE
+        kept = [key[4][1][0] for key in graph._captures]  # batch size of each kept capture
         assert kept == list(xs)[-GRAPH_CACHE_SIZE:]
         n_first = next(iter(xs))
         assert torch.equal(graph(xs[n_first]), eager(xs[n_first]))  # recaptured
-        assert len(graph._graphs) == GRAPH_CACHE_SIZE
+        assert len(graph._captures) == GRAPH_CACHE_SIZE
     assert graph.cuda_graph_replays == len(xs) + 1
+
+
+def test_evicting_a_capture_replayed_on_another_stream_waits_for_that_replay():
+    from transformer_opt.submission import GRAPH_CACHE_SIZE
+
+    torch.manual_seed(11)
+    graph = _graph_pair("graph")
+    eager = _graph_pair("eager")
+    eager.load_state_dict(graph.state_dict())
+    side = torch.cuda.Stream()
+    xs = [torch.randn(n, 128, 256, device="cuda") for n in range(1, GRAPH_CACHE_SIZE + 3)]
+    with torch.inference_mode():
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            first = graph(xs[0])  # captured and replayed on the side stream
+        # no synchronisation: the following captures on the current stream
+        # evict the first one while its replay may still be queued
+        others = [graph(x) for x in xs[1:]]
+        torch.cuda.synchronize()
+        assert torch.equal(first, eager(xs[0]))
+        for x, y in zip(xs[1:], others):
+            assert torch.equal(y, eager(x))
+    assert len(graph._captures) == GRAPH_CACHE_SIZE
+
+
+def test_device_status_turns_into_runtime_error_on_the_product_path():
+    torch.manual_seed(12)
+    model = UserOptimizedTransformer(TransformerConfig(2, 128, 256, 4, 1024, 1, False))
+    model = model.to("cuda").eval()
+    x_host = torch.randn(2, 128, 256).pin_memory()
+    _native.device_status(0, clear=True)
+    with torch.inference_mode():
+        model.forward_host(x_host)  # clear word: no error
+        model.check_device_status()
+        # a bounded wait that nothing completes (2 ms) sets a status bit
+        _native.selftest_wait_timeout(0, 2000)
+        with pytest.raises(RuntimeError, match="device status"):
+            model.check_device_status()
+        with pytest.raises(RuntimeError, match="device status"):
+            model.forward_host(x_host)
+        # clear=True reports the bit one last time and resets the word
+        with pytest.raises(RuntimeError, match="self test"):
+            model.check_device_status(clear=True)
+        model.check_device_status()
+        y = model.forward_host(x_host)
+        assert torch.equal(y, model(x_host.cuda()).cpu())

@@ -163,3 +163,39 @@ def test_forward_host_accepts_chunk_sizes_on_a_cpu_model():
     with torch.inference_mode():
         ref = model(x)
         assert torch.equal(model.forward_host(x, chunks=[1, 3]), ref)  # CPU: plain forward
+
+
+def test_tf32_weight_rounding_keeps_nan_and_rounds_like_the_hardware():
+    import struct
+
+    from transformer_opt.submission import _round_to_tf32
+
+    def rna_tf32(value: float) -> float:
+        # round to 10 explicit mantissa bits, ties away from zero, on the bits
+        (bits,) = struct.unpack("<I", struct.pack("<f", value))
+        sign, mag = bits & 0x80000000, bits & 0x7FFFFFFF
+        if mag > 0x7F800000:
+            return value  # NaN stays NaN
+        mag = min(((mag + 0x1000) & ~0x1FFF), 0x7F800000)
+        return struct.unpack("<f", struct.pack("<I", sign | mag))[0]
+
+    flt_max = torch.finfo(torch.float32).max
+    values = torch.tensor(
+        [1.0, -1.0, 1.0 + 2**-11, 1.0 + 3 * 2**-12, -(1.0 + 2**-11), flt_max, -flt_max,
+         float("inf"), float("-inf"), 1e-40, -3.14159, 65504.0, 0.0, -0.0],
+        dtype=torch.float32,
+    )
+    rounded = _round_to_tf32(values)
+    for v, r in zip(values.tolist(), rounded.tolist()):
+        assert r == rna_tf32(v) or (r != r and v != v), (v, r)
+    assert torch.isinf(rounded[5]) and rounded[5] > 0  # FLT_MAX carries to +inf
+    # NaN payloads whose integer carry would wrap into an infinity or a zero
+    nan_bits = torch.tensor([0x7FFFF000, 0x7FFFFFFF, -4096, 0x7F801000], dtype=torch.int32)
+    nans = nan_bits.view(torch.float32)
+    assert torch.isnan(_round_to_tf32(nans)).all()
+
+
+def test_check_device_status_is_a_no_op_off_cuda():
+    model = UserOptimizedTransformer(TransformerConfig(1, 8, 16, 2, 32, 1, False))
+    model.check_device_status()
+    model.check_device_status(clear=True)

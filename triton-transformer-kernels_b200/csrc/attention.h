@@ -30,6 +30,10 @@ struct AttnTcArgs {
 // Keys per tile of the tcgen05 kernel for (dtype, head_dim); the query tile
 // is always 128 rows.
 int attention_tc_block_n(int dtype, int head_dim);
+// Whether the tcgen05 kernel's work-item numbering fits in int for this
+// shape: the causal pair schedule numbers 2 * ceil(tiles / 2) items per
+// (batch, head) and looks up to 2 * grid items ahead. Host-only arithmetic.
+bool attention_tc_items_fit(int dtype, int head_dim, int64_t batch, int64_t seq, int64_t heads);
 cudaError_t launch_attention_tc(const AttnTcArgs& args, cudaStream_t stream);
 
 // Arguments of the CUDA-core route (any supported head_dim, any strides).

@@ -14,6 +14,18 @@ int attention_tc_block_n(int dtype, int head_dim) {
   return head_dim == 128 ? tc::TcTile<__half, 128>::kBN : tc::TcTile<__half, 64>::kBN;
 }
 
+bool attention_tc_items_fit(int dtype, int head_dim, int64_t batch, int64_t seq, int64_t heads) {
+  int nq = 1;
+  if (dtype != B200TK_DTYPE_FLOAT32)
+    nq = head_dim == 128 ? tc::TcTile<__half, 128>::kNQ : tc::TcTile<__half, 64>::kNQ;
+  const int64_t rows_per_item = static_cast<int64_t>(nq) * tc::BM;
+  const int64_t tiles = (seq + rows_per_item - 1) / rows_per_item;
+  // pair numbering rounds the tile count up to even; the persistent loop's
+  // next-item arithmetic adds up to 2 * grid (grid <= SM count < 1024)
+  const int64_t numbered = 2 * ((tiles + 1) / 2) * batch * heads;
+  return numbered + 2 * 1024 <= 0x7FFFFFFF;
+}
+
 cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
   tc::AttnTcParams prm;
   prm.tm_q = *reinterpret_cast<const CUtensorMap*>(a.tm_q);

@@ -1300,7 +1300,11 @@ cudaError_t launch_dtype_hd(AttnTcParams prm, int num_sms, bool causal, bool has
   const int rows_per_cta = C::kNQ * BM;
   prm.n_qtiles = (prm.seq + rows_per_cta - 1) / rows_per_cta;
   const int64_t items = static_cast<int64_t>(prm.n_qtiles) * prm.batch * prm.heads;
-  if (items > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
+  // the causal pair numbering (2 * ceil(tiles / 2) per batch-head) plus the
+  // persistent loop's look-ahead of 2 * grid must stay inside int
+  const int64_t numbered = 2 * static_cast<int64_t>((prm.n_qtiles + 1) / 2) * prm.batch * prm.heads;
+  if (items > 0x7FFFFFFF || numbered + 2 * static_cast<int64_t>(num_sms) > 0x7FFFFFFF)
+    return cudaErrorInvalidConfiguration;
   // Non-causal items all cost the same: one persistent CTA per SM loops over
   // them (barriers and TMEM set up once, the next item's loads overlap the
   // current item's tail). Causal items differ in length by up to the number

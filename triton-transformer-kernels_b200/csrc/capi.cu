@@ -180,6 +180,24 @@ int route_for(const void* q, const int64_t* qs, const void* k, const int64_t* ks
   return B200TK_ROUTE_GENERIC;
 }
 
+// The chosen kernel numbers its work items with int: reject shapes whose
+// item count would overflow (the launch would otherwise do no work and
+// report success). Rows per CTA of the generic kernel: 128 / (D / min(D, 32)).
+int check_item_range(int route, int dtype, int64_t batch, int64_t seq, int64_t heads,
+                     int64_t head_dim) {
+  bool fits;
+  if (route == B200TK_ROUTE_TCGEN05) {
+    fits = attention_tc_items_fit(dtype, static_cast<int>(head_dim), batch, seq, heads);
+  } else {
+    const int64_t rows = 128 / (head_dim / (head_dim < 32 ? head_dim : 32));
+    fits = ((seq + rows - 1) / rows) * batch * heads <= 0x7FFFFFFF;
+  }
+  if (!fits)
+    return fail(B200TK_ERR_UNSUPPORTED,
+                "batch x heads x query tiles exceeds the kernel's work-item range");
+  return B200TK_OK;
+}
+
 __global__ void selftest_wait_kernel(unsigned int* status, uint64_t limit_ns) {
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
@@ -220,8 +238,10 @@ int b200tk_attention_route(const void* q, const int64_t* q_strides, const void* 
   int rc = validate_attention(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len,
                               heads, head_dim);
   if (rc != B200TK_OK) return rc;
-  return route_for(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len, heads,
-                   head_dim);
+  const int route = route_for(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len,
+                              heads, head_dim);
+  rc = check_item_range(route, dtype, batch, seq_len, heads, head_dim);
+  return rc != B200TK_OK ? rc : route;
 }
 
 int b200tk_attention_fwd(const void* q, const int64_t* q_strides, const void* k,
@@ -237,9 +257,12 @@ int b200tk_attention_fwd(const void* q, const int64_t* q_strides, const void* k,
   if (valid_token_mask != nullptr && mask_strides == nullptr)
     return fail(B200TK_ERR_INVALID_ARGUMENT, "mask_strides must be given with a mask");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int route = route_for(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len,
-                              heads, head_dim);
-  if (route == B200TK_ROUTE_TCGEN05 && aligned16(out)) {
+  int route = route_for(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len, heads,
+                        head_dim);
+  if (route == B200TK_ROUTE_TCGEN05 && !aligned16(out)) route = B200TK_ROUTE_GENERIC;
+  rc = check_item_range(route, dtype, batch, seq_len, heads, head_dim);
+  if (rc != B200TK_OK) return rc;
+  if (route == B200TK_ROUTE_TCGEN05) {
     AttnTcArgs a;
     std::memset(&a, 0, sizeof(a));
     const int bn = attention_tc_block_n(dtype, static_cast<int>(head_dim));

@@ -6,12 +6,12 @@ same ``forward(x, valid_token_mask=None)``, same counters and the same
 state-dict surface, so the organizer harness's strict ``copy_model_weights``
 works unchanged).
 
-execution_mode: "eager" launches the fused forward op by op; "graph" captures
-it once per input signature into a CUDA graph and replays it (fresh input
-copied into the graph's static buffer, output cloned so results never alias,
-the reference's _InferenceGraph contract, submission.py:674-723); "auto"
-replays only launch-bound forwards (AUTO_GRAPH_MAX_ELEMENTS) and the chunk
-forwards of forward_host. Up to GRAPH_CACHE_SIZE captures are kept.
+execution_mode: "eager" launches the fused forward op by op; "graph" records
+it once per input signature as a CUDA graph (``_CapturedForward``) and
+replays that; "auto" replays only launch-bound forwards
+(AUTO_GRAPH_MAX_ELEMENTS) and the chunk forwards of forward_host. Results of
+a replay never alias one another (the reference's contract for its graph
+path, submission.py:674-723). Up to GRAPH_CACHE_SIZE captures are kept.
 
 On an sm_100 GPU in inference mode every layer runs
   packed QKV projection (cuBLAS, fp32) or three projections (16-bit)
@@ -28,6 +28,14 @@ only while TF32 matmuls are allowed, the precision the unfused fp32 Linear
 then has), or cuBLAS + ATen GELU. Everything else (CPU, autograd,
 training mode, backends other than the custom one) runs the explicit
 PyTorch forward with attention through ``attention_forward``.
+
+Device-side failures: the kernels bound every pipeline wait; a wait that
+gives up leaves its output undefined and sets a bit in the library's
+per-device status word. ``forward_host(synchronize=True)`` reads the word
+after the result has landed and raises ``RuntimeError`` if a bit is set;
+callers of the asynchronous ``forward`` check with ``check_device_status()``
+once their stream has been synchronised (the reference's fail-closed
+contract, transformer_opt/dispatch.py:116-123).
 """
 
 from __future__ import annotations
@@ -86,6 +94,48 @@ GRAPH_CACHE_SIZE = 4
 __all__ = ["TransformerConfig", "UserOptimizedTransformer"]
 
 
+class _RouteTally:
+    """Kernel routes taken by one fused or explicit forward.
+
+    Every helper of the forward records the route it took here; the public
+    entry points add a finished tally to the model's counters. A capture keeps
+    the tally of its set-up run and adds it once per replay, so replays count
+    exactly like eager forwards and the set-up itself counts for nothing.
+    """
+
+    __slots__ = ("attention", "residual_layer_norm", "linear_gelu")
+
+    def __init__(self) -> None:
+        self.attention: Dict[str, int] = {}
+        self.residual_layer_norm = 0
+        self.linear_gelu = 0
+
+    def add_attention(self, backend: str) -> None:
+        self.attention[backend] = self.attention.get(backend, 0) + 1
+
+    def credit(self, model: "UserOptimizedTransformer") -> None:
+        for backend, count in self.attention.items():
+            model.attention_backend_counts[backend] = (
+                model.attention_backend_counts.get(backend, 0) + count
+            )
+        model.fused_residual_layer_norm_calls += self.residual_layer_norm
+        model.fused_linear_gelu_calls += self.linear_gelu
+
+
+def _round_to_tf32(weight: torch.Tensor) -> torch.Tensor:
+    """``weight`` (fp32) rounded to the nearest TF32 value, ties away from zero.
+
+    Adding half of the dropped 13-bit field to the magnitude bits and
+    clearing the field is that rounding for every finite value and for the
+    infinities (the carry of the largest finite values makes them infinite,
+    as the hardware rounding does); NaNs are kept as they are (the integer
+    carry would turn some NaN payloads into infinities or zeros).
+    """
+    bits = weight.detach().contiguous().view(torch.int32)
+    rounded = ((bits + 0x1000) & -0x2000).view(torch.float32)
+    return torch.where(torch.isnan(weight), weight, rounded)
+
+
 class UserOptimizedTransformer(TransformerWeights):
     """Transformer inference forward routed through libb200tk.so."""
 
@@ -119,7 +169,7 @@ class UserOptimizedTransformer(TransformerWeights):
         self.fused_residual_layer_norm_calls = 0
         self.fused_linear_gelu_calls = 0
         self.cuda_graph_replays = 0
-        self._graphs: "OrderedDict[tuple, _ForwardGraph]" = OrderedDict()
+        self._captures: "OrderedDict[tuple, _CapturedForward]" = OrderedDict()
         self._host_streams: Dict[int, Tuple[torch.cuda.Stream, ...]] = {}
         # Derived, non-persistent inference data keyed by id(attention module):
         # (parameter signature, packed weight [3d, d], packed bias [3d]).
@@ -140,7 +190,7 @@ class UserOptimizedTransformer(TransformerWeights):
         state.pop("_lock", None)
         state["_packed_qkv_cache"] = {}
         state["_tf32_weight_cache"] = {}
-        state["_graphs"] = OrderedDict()
+        state["_captures"] = OrderedDict()
         state["_host_streams"] = {}
         return state
 
@@ -150,7 +200,7 @@ class UserOptimizedTransformer(TransformerWeights):
         self.__dict__.setdefault("ffn_backend", "auto")
         self.__dict__.setdefault("fused_linear_gelu_calls", 0)
         self.__dict__.setdefault("_tf32_weight_cache", {})
-        self.__dict__.setdefault("_graphs", OrderedDict())
+        self.__dict__.setdefault("_captures", OrderedDict())
 
     def _apply(self, fn, recurse=True):
         # device / dtype moves invalidate the packed projection weights and
@@ -163,7 +213,36 @@ class UserOptimizedTransformer(TransformerWeights):
     def clear_cuda_graph(self) -> None:
         """Release the cached captures; a later eligible call captures again."""
         with self._lock:
-            self._graphs.clear()
+            while self._captures:
+                self._captures.popitem(last=False)[1].release()
+
+    def check_device_status(self, clear: bool = False) -> None:
+        """Raise ``RuntimeError`` if a libb200tk kernel on this model's device
+        gave up a pipeline wait (its output is then undefined).
+
+        Synchronises the device first, so the check covers every launch made
+        so far. ``forward_host(synchronize=True)`` runs this check itself;
+        callers of ``forward`` (which returns before the GPU finishes) run it
+        when they need the result to be trusted. ``clear`` resets the status
+        word after reading it (the call still raises if it was set). A model
+        outside CUDA has nothing to check.
+        """
+        device = next(self.parameters()).device
+        if device.type != "cuda":
+            return
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        status = _native.device_status(index, clear=clear)
+        if status:
+            names = []
+            if status & _native.STATUS_PIPELINE_TIMEOUT:
+                names.append("a kernel pipeline wait timed out")
+            if status & _native.STATUS_SELFTEST_TIMEOUT:
+                names.append("the wait-timeout self test fired")
+            raise RuntimeError(
+                f"libb200tk device status {status:#x} on cuda:{index}: "
+                + "; ".join(names or ["unknown status bit"])
+                + " -- results computed since the status was last cleared are not valid"
+            )
 
     # ------------------------------------------------------------ projections
     @staticmethod
@@ -197,9 +276,7 @@ class UserOptimizedTransformer(TransformerWeights):
         signature = self._params_signature(linear.weight)
         cached = self._tf32_weight_cache.get(id(linear))
         if signature is None or cached is None or cached[0] != signature:
-            bits = linear.weight.detach().contiguous().view(torch.int32)
-            rounded = ((bits + 0x1000) & -0x2000).view(torch.float32)
-            cached = (signature, rounded)
+            cached = (signature, _round_to_tf32(linear.weight))
             if signature is not None:
                 self._tf32_weight_cache[id(linear)] = cached
         return cached[1]
@@ -236,6 +313,7 @@ class UserOptimizedTransformer(TransformerWeights):
         x: torch.Tensor,
         valid_token_mask: Optional[torch.Tensor],
         causal: bool,
+        tally: _RouteTally,
     ) -> torch.Tensor:
         batch, seq_len, _ = x.shape
         q, k, v = self._project_qkv(attn, x)
@@ -243,7 +321,7 @@ class UserOptimizedTransformer(TransformerWeights):
             q, k, v, valid_token_mask, causal=causal, scale=attn.scale,
             backend=self.attention_backend,
         )
-        self.attention_backend_counts[dispatch.selected] += 1
+        tally.add_attention(dispatch.selected)
         return attn.out_proj(context.reshape(batch, seq_len, attn.d_model))
 
     # ---------------------------------------------------------------- routing
@@ -308,11 +386,14 @@ class UserOptimizedTransformer(TransformerWeights):
         time. Sequences do not interact
         in this model: the result is the forward of each group. Pinned host
         memory makes the copies asynchronous (pageable memory works, with
-        synchronous copies). The call returns once ``out`` holds the result;
-        with ``synchronize=False`` it returns as soon as the work is queued,
-        the caller's current stream waits for all of it, and ``out`` may be
-        read after that stream is synchronised. A single chunk runs on the
-        caller's stream. On a model outside CUDA this is ``forward``.
+        synchronous copies). The call returns once ``out`` holds the result
+        and the device status word is clear (``RuntimeError`` otherwise, see
+        ``check_device_status``); with ``synchronize=False`` it returns as
+        soon as the work is queued, the caller's current stream waits for all
+        of it, and ``out`` may be read after that stream is synchronised (and,
+        to trust it, ``check_device_status()`` has passed). A single chunk
+        runs on the caller's stream. On a model outside CUDA this is
+        ``forward``.
         """
         device = next(self.parameters()).device
         if device.type != "cuda":
@@ -347,6 +428,7 @@ class UserOptimizedTransformer(TransformerWeights):
             out.copy_(self.forward(xs, ms), non_blocking=True)
             if synchronize:
                 current.synchronize()
+                self.check_device_status()
             return out
         streams = self._streams_for(device)
         # A chunk's forward is launch-bound on the host (measured on C2: ~1.4 ms
@@ -375,6 +457,7 @@ class UserOptimizedTransformer(TransformerWeights):
         if synchronize:
             for event in done:
                 event.synchronize()
+            self.check_device_status()
         return out
 
     def _chunk_forward(self, x, valid_token_mask, replay: bool) -> torch.Tensor:
@@ -383,9 +466,9 @@ class UserOptimizedTransformer(TransformerWeights):
         if replay and self.fused_route_reason(x, valid_token_mask) is None:
             if not torch.cuda.is_current_stream_capturing():
                 _native.load()
-                signature = self._graph_signature(x, valid_token_mask)
-                if signature is not None:
-                    return self._graph_forward(x, valid_token_mask, signature)
+                key = self._capture_key(x, valid_token_mask)
+                if key is not None:
+                    return self._replay(x, valid_token_mask, key)
         return self.forward(x, valid_token_mask)
 
     @staticmethod
@@ -430,14 +513,46 @@ class UserOptimizedTransformer(TransformerWeights):
         self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
     ) -> torch.Tensor:
         reason = self.fused_route_reason(x, valid_token_mask)
+        tally = _RouteTally()
         if reason is None:
             _native.load()  # on an eligible GPU a missing library is an error
             if self._graph_eligible(x):
-                signature = self._graph_signature(x, valid_token_mask)
-                if signature is not None:
-                    return self._graph_forward(x, valid_token_mask, signature)
-            return self._forward_fused(x, valid_token_mask)
-        return self._forward_eager(x, valid_token_mask)
+                key = self._capture_key(x, valid_token_mask)
+                if key is not None:
+                    return self._replay(x, valid_token_mask, key)
+            out = self._forward_fused(x, valid_token_mask, tally)
+        else:
+            out = self._forward_eager(x, valid_token_mask, tally)
+        tally.credit(self)
+        return out
+
+    def forward_layer(
+        self,
+        index: int,
+        x: torch.Tensor,
+        valid_token_mask: Optional[torch.Tensor] = None,
+    ) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Block ``index`` of the fused forward on its input residual stream.
+
+        ``x`` is what the explicit model's block ``index`` receives. Returns
+        the block's output residual stream (the explicit block's return value)
+        and the LayerNorm of it that the fused loop carries on: norm1 of the
+        next block, or final_norm (zeroed on invalid rows) after the last.
+        Runs on the fused kernels only (``ValueError`` if they do not apply)
+        and adds to the route counters like a forward of one block.
+        """
+        reason = self.fused_route_reason(x, valid_token_mask)
+        if reason is not None:
+            raise ValueError(f"forward_layer needs the fused route: {reason}")
+        if not 0 <= index < len(self.layers):
+            raise ValueError(f"layer index {index} is outside [0, {len(self.layers)})")
+        _native.load()
+        tally = _RouteTally()
+        norm1 = self.layers[index].norm1
+        normalized = layer_norm(x, norm1.weight, norm1.bias, norm1.eps)
+        result = self._fused_block(index, x, normalized, valid_token_mask, tally)
+        tally.credit(self)
+        return result
 
     # ------------------------------------------------------------ CUDA graph
     def _graph_eligible(self, x: torch.Tensor) -> bool:
@@ -447,8 +562,9 @@ class UserOptimizedTransformer(TransformerWeights):
             return True
         return x.numel() * len(self.layers) <= AUTO_GRAPH_MAX_ELEMENTS
 
-    def _graph_signature(self, x, valid_token_mask) -> Optional[tuple]:
-        """Everything a replay depends on, or None when it cannot be tracked."""
+    def _capture_key(self, x, valid_token_mask) -> Optional[tuple]:
+        """(parameter state, input signature) a capture is valid for, or None
+        when the parameter state cannot be tracked (no capture is made)."""
         params = []
         for module in self.modules():
             if module.training or module._forward_hooks or module._forward_pre_hooks:
@@ -459,35 +575,29 @@ class UserOptimizedTransformer(TransformerWeights):
                 if parameter.is_inference():
                     return None  # no version counter: in-place updates would go unseen
                 params.append((parameter.data_ptr(), parameter._version))
-        norms = tuple(
-            m.eps for m in self.modules() if isinstance(m, nn.LayerNorm)
+        eps = tuple(m.eps for m in self.modules() if isinstance(m, nn.LayerNorm))
+        inputs = (
+            x.device, tuple(x.shape), x.dtype, valid_token_mask is not None,
+            torch.backends.cuda.matmul.allow_tf32,
+            torch.is_inference_mode_enabled(),  # the boxes are inference tensors or not
         )
-        return (
-            tuple(params), norms, self.attention_backend, self.ffn_backend, x.device,
-            tuple(x.shape), x.dtype,
-            valid_token_mask is not None, torch.backends.cuda.matmul.allow_tf32,
-            torch.is_inference_mode_enabled(),  # static buffers are inference tensors or not
-        )
+        return (tuple(params), eps, self.attention_backend, self.ffn_backend, inputs)
 
-    def _graph_forward(self, x, valid_token_mask, signature) -> torch.Tensor:
+    def _replay(self, x, valid_token_mask, key) -> torch.Tensor:
         with self._lock:
-            graph = self._graphs.get(signature)
-            if graph is None:
-                # captures made with other parameters (or parameter versions)
-                # can never replay again: release them first
-                for key in [k for k in self._graphs if k[0] != signature[0]]:
-                    del self._graphs[key]
-                while len(self._graphs) >= GRAPH_CACHE_SIZE:
-                    self._graphs.popitem(last=False)
-                graph = _ForwardGraph(self, x, valid_token_mask, signature)
-                self._graphs[signature] = graph
+            capture = self._captures.get(key)
+            if capture is None:
+                # a capture of other parameter state can never be used again
+                for stale in [k for k in self._captures if k[0] != key[0]]:
+                    self._captures.pop(stale).release()
+                while len(self._captures) >= GRAPH_CACHE_SIZE:
+                    self._captures.popitem(last=False)[1].release()
+                capture = _CapturedForward(self, x, valid_token_mask)
+                self._captures[key] = capture
             else:
-                self._graphs.move_to_end(signature)
-            out = graph.replay(x, valid_token_mask)
-            for backend, count in graph.backend_counts.items():
-                self.attention_backend_counts[backend] += count
-            self.fused_residual_layer_norm_calls += graph.fused_calls
-            self.fused_linear_gelu_calls += graph.ffn_calls
+                self._captures.move_to_end(key)
+            out = capture.run(x, valid_token_mask)
+            capture.routes.credit(self)
             self.cuda_graph_replays += 1
             return out
 
@@ -498,6 +608,7 @@ class UserOptimizedTransformer(TransformerWeights):
         update: torch.Tensor,
         norm: nn.LayerNorm,
         valid_token_mask: Optional[torch.Tensor],
+        tally: _RouteTally,
         *,
         zero_invalid_residual: bool = False,
         zero_invalid_normalized: bool = False,
@@ -509,7 +620,7 @@ class UserOptimizedTransformer(TransformerWeights):
             zero_invalid_normalized=zero_invalid_normalized,
             round_normalized_tf32=round_normalized_tf32,
         )
-        self.fused_residual_layer_norm_calls += 1
+        tally.residual_layer_norm += 1
         return residual, normalized
 
     def _ffn_fused(self, linear: nn.Linear, h: torch.Tensor) -> bool:
@@ -529,7 +640,9 @@ class UserOptimizedTransformer(TransformerWeights):
         outputs = (h.numel() // h.shape[-1]) * linear.out_features
         return self.ffn_backend == "b200" or outputs >= FUSED_FFN_MIN_OUTPUTS
 
-    def _ffn_in_gelu(self, linear: nn.Linear, h: torch.Tensor, fused: bool) -> torch.Tensor:
+    def _ffn_in_gelu(
+        self, linear: nn.Linear, h: torch.Tensor, fused: bool, tally: _RouteTally
+    ) -> torch.Tensor:
         """``F.gelu(linear(h), approximate="none")`` (reference:
         submission.py:506-508), as one kernel when ``fused``. For fp32, h
         arrives rounded to TF32 (the norm2 kernel's ROUND_TF32 flag) and the
@@ -538,47 +651,60 @@ class UserOptimizedTransformer(TransformerWeights):
         if not fused:
             return F.gelu(linear(h), approximate="none")
         weight = self._tf32_weight(linear) if h.dtype == torch.float32 else linear.weight
-        self.fused_linear_gelu_calls += 1
+        tally.linear_gelu += 1
         return fused_linear_gelu(h, weight, linear.bias)
 
+    def _fused_block(
+        self,
+        index: int,
+        x: torch.Tensor,
+        normalized: torch.Tensor,
+        valid_token_mask: Optional[torch.Tensor],
+        tally: _RouteTally,
+    ) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Block ``index`` given its residual input x and norm1(x): returns the
+        block's residual output and the next LayerNorm of it."""
+        layer = self.layers[index]
+        attn_out = self._attention(
+            layer.attention, normalized, valid_token_mask, self.config.causal, tally
+        )
+        del normalized
+        fused_ffn = self._ffn_fused(layer.ffn_in, x)
+        x, ffn_input = self._fused_residual_norm(
+            x, attn_out, layer.norm2, valid_token_mask, tally,
+            round_normalized_tf32=fused_ffn and x.dtype == torch.float32,
+        )
+        del attn_out
+        ffn_out = layer.ffn_out(self._ffn_in_gelu(layer.ffn_in, ffn_input, fused_ffn, tally))
+        del ffn_input
+        is_last = index + 1 == len(self.layers)
+        next_norm = self.final_norm if is_last else self.layers[index + 1].norm1
+        # Invalid rows: the block-end masked_fill zeroes the residual stream,
+        # and the model output is zeroed after final_norm.
+        return self._fused_residual_norm(
+            x, ffn_out, next_norm, valid_token_mask, tally,
+            zero_invalid_residual=valid_token_mask is not None,
+            zero_invalid_normalized=is_last and valid_token_mask is not None,
+        )
+
     def _forward_fused(
-        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
+        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor], tally: _RouteTally
     ) -> torch.Tensor:
-        causal = self.config.causal
         first = self.layers[0].norm1
         normalized = layer_norm(x, first.weight, first.bias, first.eps)
-        for index, layer in enumerate(self.layers):
-            attn_out = self._attention(layer.attention, normalized, valid_token_mask, causal)
-            del normalized
-            fused_ffn = self._ffn_fused(layer.ffn_in, x)
-            x, ffn_input = self._fused_residual_norm(
-                x, attn_out, layer.norm2, valid_token_mask,
-                round_normalized_tf32=fused_ffn and x.dtype == torch.float32,
-            )
-            del attn_out
-            ffn_out = layer.ffn_out(self._ffn_in_gelu(layer.ffn_in, ffn_input, fused_ffn))
-            del ffn_input
-            is_last = index + 1 == len(self.layers)
-            next_norm = self.final_norm if is_last else self.layers[index + 1].norm1
-            # Invalid rows: the block-end masked_fill zeroes the residual
-            # stream, and the model output is zeroed after final_norm.
-            x, normalized = self._fused_residual_norm(
-                x, ffn_out, next_norm, valid_token_mask,
-                zero_invalid_residual=valid_token_mask is not None,
-                zero_invalid_normalized=is_last and valid_token_mask is not None,
-            )
-            del ffn_out
+        for index in range(len(self.layers)):
+            x, normalized = self._fused_block(index, x, normalized, valid_token_mask, tally)
         return normalized
 
     # ----------------------------------------------------------------- eager
     def _forward_eager(
-        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
+        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor], tally: _RouteTally
     ) -> torch.Tensor:
         causal = self.config.causal
         for layer in self.layers:
             x = explicit_block(
                 layer, x, valid_token_mask, causal,
-                lambda attn, h: self._attention(attn, h, valid_token_mask, causal),
+                lambda attn, h: self._attention(attn, h, valid_token_mask, causal, tally),
             )
         x = self.final_norm(x)
         if valid_token_mask is not None:
@@ -586,56 +712,58 @@ class UserOptimizedTransformer(TransformerWeights):
         return x
 
 
-class _ForwardGraph:
-    """One captured fused forward with its own static input and output."""
+class _CapturedForward:
+    """The fused forward of one input signature, recorded as a CUDA graph.
 
-    def __init__(self, model, x, valid_token_mask, signature) -> None:
-        self.signature = signature
-        self.x = x.clone()
-        self.mask = valid_token_mask.clone() if valid_token_mask is not None else None
-        counts_before = dict(model.attention_backend_counts)
-        fused_before = model.fused_residual_layer_norm_calls
-        ffn_before = model.fused_linear_gelu_calls
-        stream = torch.cuda.Stream(device=x.device)
-        current = torch.cuda.current_stream(x.device)
-        stream.wait_stream(current)
-        try:
-            with torch.cuda.stream(stream):
-                # warm-up outside capture: builds packed weights and resolves
-                # the library's per-device state
-                model._forward_fused(self.x, self.mask)
-            current.wait_stream(stream)
-            capture_counts = dict(model.attention_backend_counts)
-            capture_fused = model.fused_residual_layer_norm_calls
-            capture_ffn = model.fused_linear_gelu_calls
-            self.graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.graph, stream=stream):
-                self.out = model._forward_fused(self.x, self.mask)
-            current.wait_stream(stream)
-            self.backend_counts = {
-                k: v - capture_counts[k] for k, v in model.attention_backend_counts.items()
-            }
-            self.fused_calls = model.fused_residual_layer_norm_calls - capture_fused
-            self.ffn_calls = model.fused_linear_gelu_calls - capture_ffn
-            # keep the packed weights the graph reads alive
-            self.packed = tuple(model._packed_qkv_cache.values()) + tuple(
-                model._tf32_weight_cache.values()
-            )
-            self.done = torch.cuda.Event()
-            self.done.record(current)
-        finally:
-            # warm-up and capture are set-up, not user-visible forwards
-            model.attention_backend_counts = counts_before
-            model.fused_residual_layer_norm_calls = fused_before
-            model.fused_linear_gelu_calls = ffn_before
+    Memory: the graph's input and output tensors ("boxes") are allocated
+    while the graph is being recorded, so they belong to the graph's private
+    memory pool together with every intermediate. The caching allocator hands
+    that pool's memory to nothing else until the graph is gone and the pool is
+    freed (cudaFree, which waits for the device), so no stream can reuse a box
+    while a replay on another stream still reads or writes it. ``release``
+    additionally waits for the last replay before the object is dropped.
 
-    def replay(self, x, valid_token_mask) -> torch.Tensor:
-        current = torch.cuda.current_stream(x.device)
-        current.wait_event(self.done)
-        self.x.copy_(x)
-        if self.mask is not None:
-            self.mask.copy_(valid_token_mask)
+    Counting: the set-up run (needed before recording: it resolves the
+    library's per-device state, selects cuBLAS kernels and builds the cached
+    packed weights) records its routes in ``routes``; the model credits that
+    tally once per replay, and the set-up and the recording credit nothing.
+    """
+
+    def __init__(self, model: UserOptimizedTransformer, x, valid_token_mask) -> None:
+        device = x.device
+        caller = torch.cuda.current_stream(device)
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(caller)
+        self.routes = _RouteTally()
+        with torch.cuda.stream(side):
+            model._forward_fused(x, valid_token_mask, self.routes)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=side):
+            self.x_box = torch.empty_like(x)
+            self.mask_box = None if valid_token_mask is None else torch.empty_like(valid_token_mask)
+            self.y_box = model._forward_fused(self.x_box, self.mask_box, _RouteTally())
+        caller.wait_stream(side)
+        # weights the graph reads that the model caches rather than owns
+        self.cached_weights = [entry[1:] for entry in model._packed_qkv_cache.values()]
+        self.cached_weights += [entry[1] for entry in model._tf32_weight_cache.values()]
+        # completion of the most recent use of the boxes (any stream)
+        self.boxes_free = torch.cuda.Event()
+        self.boxes_free.record(caller)
+
+    def run(self, x, valid_token_mask) -> torch.Tensor:
+        """Replay on the current stream; returns a fresh tensor (never a box)."""
+        stream = torch.cuda.current_stream(x.device)
+        # a replay queued on another stream may still be using the boxes
+        stream.wait_event(self.boxes_free)
+        self.x_box.copy_(x)
+        if self.mask_box is not None:
+            self.mask_box.copy_(valid_token_mask)
         self.graph.replay()
-        out = self.out.clone()  # later replays must not overwrite a returned result
-        self.done.record(current)
-        return out
+        result = torch.empty_like(self.y_box)
+        result.copy_(self.y_box)
+        self.boxes_free.record(stream)
+        return result
+
+    def release(self) -> None:
+        """Wait until no replay is still in flight (before the graph is dropped)."""
+        self.boxes_free.synchronize()
