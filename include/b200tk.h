@@ -58,6 +58,19 @@ extern "C" {
 #define B200TK_STATUS_PIPELINE_TIMEOUT 1u /* an mbarrier wait hit its iteration/time limit */
 #define B200TK_STATUS_SELFTEST_TIMEOUT 2u /* set only by b200tk_selftest_wait_timeout */
 
+/* Softmax schedules of the 16-bit tensor-core attention
+ * (b200tk_attention_fwd_scheduled). TWO_PASS computes every row's maximum and
+ * sum first and then rounds the already normalised probabilities to the
+ * input dtype before P@V -- the explicit reference's rounding boundary, at
+ * the cost of a second Q K^T and a second exp per score. ONE_PASS is the
+ * online softmax: unnormalised probabilities are rounded to the input dtype
+ * and the output is divided by the row sum at the end (one Q K^T, one exp).
+ * AUTO picks per call (b200tk_attention_fwd). float32 always runs its single
+ * 3xTF32 schedule; the CUDA-core route is always online. */
+#define B200TK_SCHEDULE_AUTO 0
+#define B200TK_SCHEDULE_TWO_PASS 1
+#define B200TK_SCHEDULE_ONE_PASS 2
+
 /* Attention kernel routes reported by b200tk_attention_route. */
 #define B200TK_ROUTE_TCGEN05 1 /* TMA + tcgen05.mma + TMEM pipeline */
 #define B200TK_ROUTE_GENERIC 2 /* CUDA-core kernel for shapes outside the tcgen05 envelope */
@@ -96,6 +109,22 @@ B200TK_API int b200tk_attention_fwd(const void* q, const int64_t* q_strides, con
                          const uint8_t* valid_token_mask, const int64_t* mask_strides,
                          void* out, int dtype, int64_t batch, int64_t seq_len, int64_t heads,
                          int64_t head_dim, int causal, float scale, void* stream);
+
+/*
+ * b200tk_attention_fwd with an explicit softmax schedule for 16-bit inputs
+ * (B200TK_SCHEDULE_*; AUTO is b200tk_attention_fwd itself). A schedule
+ * outside that set is B200TK_ERR_INVALID_ARGUMENT; ONE_PASS with scale <= 0
+ * runs TWO_PASS.
+ *
+ * Replaces: the same reference kernel as b200tk_attention_fwd; the schedule
+ * choice has no counterpart there (its fp16 kernel is online,
+ * attention.py:236-247).
+ */
+B200TK_API int b200tk_attention_fwd_scheduled(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides, const uint8_t* valid_token_mask,
+    const int64_t* mask_strides, void* out, int dtype, int64_t batch, int64_t seq_len,
+    int64_t heads, int64_t head_dim, int causal, float scale, int schedule, void* stream);
 
 /*
  * Which kernel b200tk_attention_fwd would launch for these arguments

@@ -24,12 +24,18 @@ struct AttnTcArgs {
   int dtype;
   int causal;
   float scale;
+  int schedule;  // B200TK_SCHEDULE_*
   unsigned int* status;
 };
 
 // Keys per tile of the tcgen05 kernel for (dtype, head_dim); the query tile
 // is always 128 rows.
 int attention_tc_block_n(int dtype, int head_dim);
+// Sequence length from which B200TK_SCHEDULE_AUTO runs 16-bit inputs on the
+// one-pass schedule; shorter sequences keep the two-pass schedule.
+constexpr int64_t kOnePassMinSeq = int64_t(1) << 62;
+// Whether a 16-bit tcgen05 launch takes the one-pass schedule.
+bool attention_tc_one_pass(int dtype, int64_t seq, float scale, int schedule);
 // Whether the tcgen05 kernel's work-item numbering fits in int for this
 // shape: the causal pair schedule numbers 2 * ceil(tiles / 2) items per
 // (batch, head) and looks up to 2 * grid items ahead. Host-only arithmetic.

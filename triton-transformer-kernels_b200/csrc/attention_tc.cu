@@ -14,6 +14,15 @@ int attention_tc_block_n(int dtype, int head_dim) {
   return head_dim == 128 ? tc::TcTile<__half, 128>::kBN : tc::TcTile<__half, 64>::kBN;
 }
 
+bool attention_tc_one_pass(int dtype, int64_t seq, float scale, int schedule) {
+  // fp32 has one schedule (3xTF32, one pass). The 16-bit one-pass kernel
+  // finds row maxima before scaling, which needs scale > 0.
+  if (dtype == B200TK_DTYPE_FLOAT32 || !(scale > 0.f)) return false;
+  if (schedule == B200TK_SCHEDULE_ONE_PASS) return true;
+  if (schedule == B200TK_SCHEDULE_TWO_PASS) return false;
+  return seq >= kOnePassMinSeq;
+}
+
 bool attention_tc_items_fit(int dtype, int head_dim, int64_t batch, int64_t seq, int64_t heads) {
   int nq = 1;
   if (dtype != B200TK_DTYPE_FLOAT32)
@@ -47,6 +56,7 @@ cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
   int exponent = 0;
   prm.scale_pow2 = a.dtype == B200TK_DTYPE_BFLOAT16 && a.scale > 0.f &&
                    std::frexp(a.scale, &exponent) == 0.5f;
+  prm.one_pass = attention_tc_one_pass(a.dtype, a.seq, a.scale, a.schedule) ? 1 : 0;
   prm.status = a.status;
   const bool causal = a.causal != 0;
   const bool has_mask = a.mask != nullptr;

@@ -71,6 +71,7 @@ struct __align__(64) AttnTcParams {
   int causal_reverse;  // schedule longest causal tiles first
   int causal_pairs;    // persistent causal schedule over (long, short) tile pairs
   int scale_pow2;      // bf16 only: scale is an exact power of two
+  int one_pass;        // 16-bit only: online softmax (see TcLayout::kTwoPass)
   unsigned int* status;
 };
 
@@ -179,7 +180,12 @@ __device__ __forceinline__ uint32_t max_pack2(uint32_t a, uint32_t b) {
   return d;
 }
 
-template <typename T, int D, int BN, int KST, int VST, int NQ>
+// OP (16-bit types only) selects the one-pass schedule: online softmax, P
+// rounded to T before normalisation. Without it 16-bit types take two passes
+// (row statistics first, then normalised P rounded to T: the explicit
+// reference's rounding boundary). fp32 always takes one pass (3xTF32 keeps P
+// at ~fp32 precision, so normalising at the end is equivalent).
+template <typename T, int D, int BN, int KST, int VST, int NQ, bool OP = false>
 struct TcLayout {
   static constexpr bool kSplit = ElemTraits<T>::kSplit;
   // Score buffers per query tile: two whenever TMEM holds them (the next
@@ -201,15 +207,19 @@ struct TcLayout {
   static constexpr int kKStage = kCopies * kKVBytes;
   static constexpr int kV = kK + KST * kKStage;
   static constexpr int kVStage = kCopies * kKVBytes;
-  static constexpr bool kTwoPass = !kSplit;
-  // Every score row is shared by two threads, each owning BN/2 keys.
+  static constexpr bool kTwoPass = !kSplit && !OP;
+  static constexpr bool kOnePass16 = !kSplit && OP;
+  // Softmax threads per score row: 16-bit two-pass: two, each owning BN/2
+  // keys (32x32b TMEM shape); one-pass and fp32: a warp covers 16 rows with
+  // four threads per row (16x256b shape), two warps per 32-lane quadrant --
+  // also 256 threads per query tile.
   static constexpr int kThreadsPerRow = 2;
   static constexpr int kSoftmaxWarpsPerTile = 4 * kThreadsPerRow;
   static constexpr int kSoftmaxWarps = NQ * kSoftmaxWarpsPerTile;
   // 16-bit (max, sum) exchange at the end of pass 1, float2 per thread (fp32
   // combines its row statistics with shuffles and needs none)
   static constexpr int kStats = kV + VST * kVStage;
-  static constexpr int kBar = kStats + (kSplit ? 0 : NQ * kThreadsPerRow * BM * 8);
+  static constexpr int kBar = kStats + (kTwoPass ? NQ * kThreadsPerRow * BM * 8 : 0);
   // fp32 P layout. kPAlias: P hi is written back into the score buffer it
   // came from and every score buffer has a P-lo buffer of its own, so the
   // softmax stores P_j while P@V_{j-1} still runs (one pv_done barrier per
@@ -272,10 +282,11 @@ struct TcLayout {
   static_assert(!kSplit || NQ == 1, "fp32 keeps one query tile per CTA");
 };
 
-template <typename T, int D, int BN, int KST, int VST, int NQ, bool CAUSAL, bool HAS_MASK>
-__global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
+template <typename T, int D, int BN, int KST, int VST, int NQ, bool OP, bool CAUSAL,
+          bool HAS_MASK>
+__global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads, 1)
     attention_fwd_tc_kernel(const __grid_constant__ AttnTcParams p) {
-  using L = TcLayout<T, D, BN, KST, VST, NQ>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ, OP>;
   constexpr bool kSplit = L::kSplit;
   constexpr int NSB = L::kNSB;
   constexpr bool kTwoPass = L::kTwoPass;
@@ -651,9 +662,12 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
               // its BN/2 keys into the first BN/4 columns of its own half of
               // the score buffer.
               constexpr int kStepsPerHalf = BN / 2 / L::kUmmaK;
+              // One-pass 16-bit P is packed contiguously (column c holds keys
+              // 2c, 2c + 1).
               const uint32_t a_tmem =
-                  kSplit ? p_tmem + ks * 8
-                         : p_tmem + (ks / kStepsPerHalf) * (BN / 2) + (ks % kStepsPerHalf) * 8;
+                  (kSplit || L::kOnePass16)
+                      ? p_tmem + ks * 8
+                      : p_tmem + (ks / kStepsPerHalf) * (BN / 2) + (ks % kStepsPerHalf) * 8;
               const uint32_t acc = (j > 0 || pass > 0 || ks > 0) ? 1u : 0u;
               if constexpr (kSplit)
                 mma_ts_tf32(o_tmem, a_tmem, bdesc, idesc_pv, acc);
@@ -699,7 +713,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         for (int g = 0; g < w.n_s && ok; ++g) {
           for (int t = 0; t < NQ && ok; ++t) {
             ok = wait_p(t, g);
-            if (ok && g >= w.n_kv) ok = issue_pv(t, g);
+            if (ok && (!kTwoPass || g >= w.n_kv)) ok = issue_pv(t, g);
             if (ok && g + NSB < w.n_s) ok = issue_s(t, g + NSB);
           }
         }
@@ -1024,6 +1038,228 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
         kc += w.n_s;
         vc += w.n_kv;
       }
+    } else if constexpr (L::kOnePass16) {
+      // ------------------------------------------ softmax, 16-bit (one pass)
+      // warp = 8t + 4 * blk + quad: query tile t, rows 32 * quad + 16 * blk
+      // .. + 15 (TMEM lane quadrant `quad`, 16-lane block `blk`). Scores are
+      // read with the 16x256b shape (lane i: rows i / 4 and i / 4 + 8 of the
+      // block, columns 8g + 2(i % 4) and + 1 of every 8-column group g), so
+      // the four threads of a row are lanes 4r .. 4r + 3 and combine row
+      // maxima and sums with shuffles. P goes back into the first BN / 2
+      // columns of the score buffer as packed T pairs (column c: keys 2c,
+      // 2c + 1) with the 16x128b shape (lane i: rows i / 4, i / 4 + 8, column
+      // 4g + i % 4 of every 4-column group g): the key pair (8g + 2(i % 4),
+      // + 1) a thread holds is exactly that column, so the packed registers
+      // are stored in the order they are produced.
+      //
+      // Online softmax: the running row maximum m_ref (log2 units) moves only
+      // when a tile's maximum exceeds it by more than kRescaleThreshold, so
+      // P <= 2^8 and O / l are rescaled rarely. The reference's dtype
+      // boundaries are kept: scores T(T(qk) * scale), probabilities rounded
+      // to T before P@V (unnormalised here; normalised by 1 / l at the end).
+      //
+      // Ordering: the score MMA of step j is committed after the P@V of step
+      // j - 1 of the same query tile (one MMA-issuing thread), so once
+      // s_full(t, j) has completed, P_{j-1} has been read (its columns may be
+      // overwritten) and O_t is not being written (a rescale may read and
+      // write it). The final pv_done wait is at most one phase behind for the
+      // same reason.
+      constexpr int kRep = BN / 8;  // 16x256b repetitions per score tile
+      constexpr int NE = 4 * kRep;  // scores per thread: 2 rows x BN / 4 keys
+      constexpr int NP = NE / 2;    // packed pairs per thread
+      static_assert(BN == 128, "one-pass 16-bit tiles are 128 keys wide");
+      static_assert(NSB == 1, "the ordering argument above assumes one score buffer per tile");
+      const int t = warp >> 3;
+      const int blk = (warp >> 2) & 1;
+      const int quad = warp & 3;
+      const int rb = quad * 32 + blk * 16;  // first row of this warp's block
+      const int ra = rb + (lane >> 2);      // this thread's rows: ra and ra + 8
+      const int cq = 2 * (lane & 3);
+      const uint32_t lane_off = static_cast<uint32_t>(rb) << 16;
+      auto e_row = [&](int e) { return ra + 8 * ((e >> 1) & 1); };
+      auto e_col = [&](int e) { return 8 * (e >> 2) + cq + (e & 1); };
+      const float scale = p.scale;
+      const bool pow2 = std::is_same_v<T, __nv_bfloat16> && p.scale_pow2 != 0;
+      // T(qk) * scale * log2e in one rounding when scale is a power of two
+      const float scale_log2e = scale * kLog2e;
+      constexpr uint32_t kNegInf2 = std::is_same_v<T, __half> ? 0xFC00FC00u : 0xFF80FF80u;
+      bool ok = true;
+      int kc = 0, vc = 0;
+      for (int it = first_item(), k = 0; it < total_items && ok; it = next_item(it), ++k) {
+        const Item w = item_at(it);
+        const int row0 = w.q0 + t * BM;
+        float m_ref[2] = {-INFINITY, -INFINITY};  // running row maxima, log2 units
+        float l_sum[2] = {0.f, 0.f};              // partial sums of this thread's columns
+
+        for (int j = 0; j < w.n_s && ok; ++j) {
+          const int sg = kc + j;
+          const int buf = sg % NSB;
+          ok = __all_sync(0xFFFFFFFFu, wait(bar_s_full(t, buf), (sg / NSB) & 1));
+          if (!ok) break;
+          tc_fence_after();
+          const int n0 = j * BN;
+          uint32_t pk[NP];  // T(qk) pairs; pair i belongs to row ra + 8 * (i & 1)
+          {
+            uint32_t raw[NE];
+            tmem_ld16x256b<8>(tmem + lane_off + L::t_s(t, buf), raw);
+            tmem_ld16x256b<8>(tmem + lane_off + L::t_s(t, buf) + 64, raw + NE / 2);
+            uint32_t kbits[BN / 32];
+            if constexpr (HAS_MASK) {
+#pragma unroll
+              for (int wd = 0; wd < BN / 32; ++wd) {
+                const int n = n0 + wd * 32 + lane;
+                bool valid = false;
+                if (n < p.seq) valid = p.mask[w.b * p.mask_sb + n * p.mask_ss] != 0;
+                kbits[wd] = __ballot_sync(0xFFFFFFFFu, valid);
+              }
+            }
+            tc_wait_ld();
+            bool pad = false;
+            if constexpr (HAS_MASK) {
+#pragma unroll
+              for (int wd = 0; wd < BN / 32; ++wd) pad = pad || kbits[wd] != 0xFFFFFFFFu;
+            }
+            const bool masked = pad || (n0 + BN > p.seq) || (CAUSAL && n0 + BN - 1 > row0 + rb);
+            if (masked) {
+#pragma unroll
+              for (int e = 0; e < NE; ++e) {
+                const int c = e_col(e);
+                const int n = n0 + c;
+                bool allowed;
+                if constexpr (HAS_MASK)
+                  allowed = (kbits[c / 32] >> (c % 32)) & 1u;
+                else
+                  allowed = n < p.seq;
+                if (CAUSAL) allowed = allowed && (n <= row0 + e_row(e));
+                raw[e] = allowed ? raw[e] : __float_as_uint(-INFINITY);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < NP; ++i)
+              pk[i] = cvt_pack2<T>(__uint_as_float(raw[2 * i]), __uint_as_float(raw[2 * i + 1]));
+          }
+          // Row maxima of T(qk) on the packed pairs (exact); T(T(qk) * scale)
+          // is monotone in T(qk), so the row maximum of the scores is T(max *
+          // scale).
+          uint32_t mx2[2] = {kNegInf2, kNegInf2};
+#pragma unroll
+          for (int i = 0; i < NP; ++i) mx2[i & 1] = max_pack2<T>(mx2[i & 1], pk[i]);
+          float mx[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float a, c;
+            unpack2<T>(mx2[h], a, c);
+            float m = fmaxf(a, c) * scale;
+            if (!pow2) {
+              float z = m;
+              round_pair<T>(m, z);
+            }
+            m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+            mx[h] = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+          }
+          float m_new[2], alpha[2] = {1.f, 1.f};
+#pragma unroll
+          for (int h = 0; h < 2; ++h) m_new[h] = fmaxf(m_ref[h], mx[h] * kLog2e);  // -inf stays
+          bool rescale = false;
+          if (j == 0) {
+            m_ref[0] = m_new[0];
+            m_ref[1] = m_new[1];
+          } else if (__any_sync(0xFFFFFFFFu, m_new[0] > m_ref[0] + kRescaleThreshold ||
+                                                 m_new[1] > m_ref[1] + kRescaleThreshold)) {
+            // a running max grew by more than 2^8: move every row of this
+            // warp to its new max (rows whose max did not grow keep alpha = 1)
+            rescale = true;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (m_new[h] > m_ref[h]) {
+                alpha[h] = ex2_approx(m_ref[h] - m_new[h]);
+                m_ref[h] = m_new[h];
+              }
+              l_sum[h] *= alpha[h];
+            }
+          }
+          if (rescale) {
+            // O_t is quiescent here (see "Ordering" above)
+#pragma unroll 1
+            for (int c = 0; c < D / 64; ++c) {
+              uint32_t o[32];
+              const uint32_t addr = tmem + lane_off + L::t_o(t) + c * 64;
+              tmem_ld16x256b<8>(addr, o);
+              tc_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha[(e >> 1) & 1]);
+              tmem_st16x256b<8>(addr, o);
+            }
+          }
+          const float m_use[2] = {m_ref[0] == -INFINITY ? 0.f : m_ref[0],
+                                  m_ref[1] == -INFINITY ? 0.f : m_ref[1]};
+          float part[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            const int h = i & 1;
+            float a, c;
+            unpack2<T>(pk[i], a, c);
+            if (pow2) {
+              fma2(a, c, scale_log2e, scale_log2e, -m_use[h], -m_use[h]);
+            } else {
+              mul2(a, c, scale, scale);
+              round_pair<T>(a, c);
+              fma2(a, c, kLog2e, kLog2e, -m_use[h], -m_use[h]);
+            }
+            a = ex2_approx(a);
+            c = ex2_approx(c);
+            add2(part[h][0], part[h][1], a, c);
+            pk[i] = cvt_pack2<T>(a, c);
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) l_sum[h] += part[h][0] + part[h][1];
+          tmem_st16x128b_x16(tmem + lane_off + L::t_s(t, buf), pk);
+          tc_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar_p_full(t, buf));
+        }
+
+        // epilogue: row sums over the row's four threads (every thread adds
+        // the same pairs: the result is bitwise the same on all four), then
+        // this thread's columns of O for its two rows, rounded to T
+        float out_scale[2] = {0.f, 0.f};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float l = l_sum[h] + __shfl_xor_sync(0xFFFFFFFFu, l_sum[h], 1);
+          l = l + __shfl_xor_sync(0xFFFFFFFFu, l, 2);
+          out_scale[h] = l > 0.f ? 1.f / l : 0.f;
+        }
+        if (ok) ok = __all_sync(0xFFFFFFFFu, wait(bar_pv_done(t, 0), (vc + w.n_kv - 1) & 1));
+        if (ok) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t o[32];
+            tmem_ld16x256b<8>(tmem + lane_off + L::t_o(t) + c * 64, o);
+            tc_wait_ld();
+            if (c == D / 64 - 1) {
+              // O has been read: the next item's first P@V may overwrite it
+              tc_fence_before();
+              mbar_arrive(bar_o_empty(t));
+            }
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const int m = row0 + e_row(e);
+              if (m < p.seq) {
+                T* dst = reinterpret_cast<T*>(p.out) +
+                         ((static_cast<int64_t>(w.b) * p.seq + m) * p.heads + w.h) * D + c * 64 +
+                         e_col(e);
+                const float sc = out_scale[(e >> 1) & 1];
+                *reinterpret_cast<uint32_t*>(dst) =
+                    cvt_pack2<T>(__uint_as_float(o[e]) * sc, __uint_as_float(o[e + 1]) * sc);
+              }
+            }
+          }
+        }
+        kc += w.n_s;
+        vc += w.n_kv;
+      }
     } else {
       // ------------------------------------------ softmax, fp32 (one pass)
       // warp = 4 * blk + quad: rows 32 * quad + 16 * blk .. + 15 of the query
@@ -1251,10 +1487,11 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ>::kThreads, 1)
   }
 }
 
-template <typename T, int D, int BN, int KST, int VST, int NQ, bool CAUSAL, bool HAS_MASK>
+template <typename T, int D, int BN, int KST, int VST, int NQ, bool OP, bool CAUSAL,
+          bool HAS_MASK>
 cudaError_t launch_tc(const AttnTcParams& prm, int grid, cudaStream_t stream) {
-  using L = TcLayout<T, D, BN, KST, VST, NQ>;
-  auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, CAUSAL, HAS_MASK>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ, OP>;
+  auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, OP, CAUSAL, HAS_MASK>;
   // at least ~116 KB so that one CTA (and one TMEM allocation) owns each SM
   const int smem = L::kBytes > 118 * 1024 ? L::kBytes : 118 * 1024;
   // The opt-in shared-memory size is set once per device and instantiation,
@@ -1291,8 +1528,23 @@ struct TcTile<float, 128> {
   static constexpr int kNQ = 1, kBN = 32, kKST = 2, kVST = 2;
 };
 
+template <typename T, int D, bool OP>
+cudaError_t launch_variant(const AttnTcParams& prm, int grid, bool causal, bool has_mask,
+                           cudaStream_t stream) {
+  using C = TcTile<T, D>;
+  if (causal)
+    return has_mask
+               ? launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, OP, true, true>(prm, grid, stream)
+               : launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, OP, true, false>(prm, grid,
+                                                                                   stream);
+  return has_mask
+             ? launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, OP, false, true>(prm, grid, stream)
+             : launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, OP, false, false>(prm, grid,
+                                                                                  stream);
+}
+
 // Fills the grid-dependent parameters and launches the instantiation for
-// (causal, mask).
+// (schedule, causal, mask).
 template <typename T, int D>
 cudaError_t launch_dtype_hd(AttnTcParams prm, int num_sms, bool causal, bool has_mask,
                             cudaStream_t stream) {
@@ -1316,13 +1568,10 @@ cudaError_t launch_dtype_hd(AttnTcParams prm, int num_sms, bool causal, bool has
     work = static_cast<int64_t>((prm.n_qtiles + 1) / 2) * prm.batch * prm.heads;
   const bool persistent = !causal || prm.causal_pairs;
   const int grid = static_cast<int>(persistent ? (work < num_sms ? work : num_sms) : work);
-  if (causal)
-    return has_mask
-               ? launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, true, true>(prm, grid, stream)
-               : launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, true, false>(prm, grid, stream);
-  return has_mask
-             ? launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, false, true>(prm, grid, stream)
-             : launch_tc<T, D, C::kBN, C::kKST, C::kVST, C::kNQ, false, false>(prm, grid, stream);
+  if constexpr (!std::is_same_v<T, float>) {
+    if (prm.one_pass) return launch_variant<T, D, true>(prm, grid, causal, has_mask, stream);
+  }
+  return launch_variant<T, D, false>(prm, grid, causal, has_mask, stream);
 }
 
 // Explicit instantiations live in attention_tc_inst.cu, compiled once per

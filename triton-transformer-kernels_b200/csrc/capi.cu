@@ -249,6 +249,22 @@ int b200tk_attention_fwd(const void* q, const int64_t* q_strides, const void* k,
                          const uint8_t* valid_token_mask, const int64_t* mask_strides, void* out,
                          int dtype, int64_t batch, int64_t seq_len, int64_t heads,
                          int64_t head_dim, int causal, float scale, void* stream) {
+  return b200tk_attention_fwd_scheduled(q, q_strides, k, k_strides, v, v_strides,
+                                        valid_token_mask, mask_strides, out, dtype, batch,
+                                        seq_len, heads, head_dim, causal, scale,
+                                        B200TK_SCHEDULE_AUTO, stream);
+}
+
+int b200tk_attention_fwd_scheduled(const void* q, const int64_t* q_strides, const void* k,
+                                   const int64_t* k_strides, const void* v,
+                                   const int64_t* v_strides, const uint8_t* valid_token_mask,
+                                   const int64_t* mask_strides, void* out, int dtype,
+                                   int64_t batch, int64_t seq_len, int64_t heads,
+                                   int64_t head_dim, int causal, float scale, int schedule,
+                                   void* stream) {
+  if (schedule != B200TK_SCHEDULE_AUTO && schedule != B200TK_SCHEDULE_TWO_PASS &&
+      schedule != B200TK_SCHEDULE_ONE_PASS)
+    return fail(B200TK_ERR_INVALID_ARGUMENT, "unknown attention schedule");
   int rc = validate_attention(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len,
                               heads, head_dim);
   if (rc != B200TK_OK) return rc;
@@ -292,6 +308,7 @@ int b200tk_attention_fwd(const void* q, const int64_t* q_strides, const void* k,
     a.dtype = dtype;
     a.causal = causal;
     a.scale = scale;
+    a.schedule = schedule;
     cudaError_t err = launch_attention_tc(a, st);
     if (err != cudaSuccess) return cuda_fail(err, "attention tcgen05 launch");
     return B200TK_OK;

@@ -456,6 +456,24 @@ __device__ __forceinline__ void tmem_st16x256b(uint32_t taddr, const uint32_t* r
   }
 }
 
+// 16 lanes x 128-bit rows (16x128b), 16 repetitions of 4 columns (64
+// columns): lane t writes rows t / 4 and t / 4 + 8 of the 16-lane block at
+// the address's lane, column 4 * g + t % 4 of repetition g; its registers
+// are (row a, rep 0), (row b, rep 0), (row a, rep 1), ... (the fragment of
+// CUTLASS's SM100_TMEM_STORE_16dp128b16x).
+__device__ __forceinline__ void tmem_st16x128b_x16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x128b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
 // Hardware base-2 exponential (MUFU.EX2), flush-to-zero; exp2(-inf) = 0.
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

@@ -33,6 +33,8 @@ RLN_ROUND_TF32 = 8
 STATUS_PIPELINE_TIMEOUT = 1
 STATUS_SELFTEST_TIMEOUT = 2
 
+SCHEDULES = {"auto": 0, "two_pass": 1, "one_pass": 2}
+
 ROUTE_TCGEN05 = 1
 ROUTE_GENERIC = 2
 
@@ -48,6 +50,11 @@ SIGNATURES = {
         _I,
         [_P, _I64P, _P, _I64P, _P, _I64P, _P, _I64P, _P, _I, _I64, _I64, _I64, _I64, _I,
          ctypes.c_float, _P],
+    ),
+    "b200tk_attention_fwd_scheduled": (
+        _I,
+        [_P, _I64P, _P, _I64P, _P, _I64P, _P, _I64P, _P, _I, _I64, _I64, _I64, _I64, _I,
+         ctypes.c_float, _I, _P],
     ),
     "b200tk_attention_route": (_I, [_P, _I64P, _P, _I64P, _P, _I64P, _I, _I64, _I64, _I64, _I64]),
     "b200tk_residual_layer_norm_fwd": (
@@ -138,8 +145,12 @@ def attention_fwd(
     out: torch.Tensor,
     causal: bool,
     scale: float,
+    schedule: str = "auto",
 ) -> None:
-    """Launch fused attention on the current stream of q's device."""
+    """Launch fused attention on the current stream of q's device.
+
+    ``schedule`` picks the 16-bit softmax schedule ("auto", "two_pass",
+    "one_pass"; see B200TK_SCHEDULE_* in include/b200tk.h)."""
     lib = load()
     b, s, h, d = q.shape
     qs, ks, vs = _strides(q.stride()[:3]), _strides(k.stride()[:3]), _strides(v.stride()[:3])
@@ -147,14 +158,16 @@ def attention_fwd(
     if mask is not None:
         mptr = ctypes.c_void_p(mask.data_ptr())
         ms = _strides(mask.stride())
-    rc = lib.b200tk_attention_fwd(
+    if schedule not in SCHEDULES:
+        raise ValueError(f"schedule must be one of {tuple(SCHEDULES)}, got {schedule!r}")
+    rc = lib.b200tk_attention_fwd_scheduled(
         ctypes.c_void_p(q.data_ptr()), qs,
         ctypes.c_void_p(k.data_ptr()), ks,
         ctypes.c_void_p(v.data_ptr()), vs,
         mptr, ms,
         ctypes.c_void_p(out.data_ptr()),
         DTYPE_CODES[q.dtype], b, s, h, d,
-        1 if causal else 0, float(scale),
+        1 if causal else 0, float(scale), SCHEDULES[schedule],
         _stream_handle(q.device),
     )
     _check(rc)

@@ -34,8 +34,15 @@ def b200_attention(
     *,
     causal: bool = False,
     scale: Optional[float] = None,
+    schedule: str = "auto",
 ) -> torch.Tensor:
-    """Run the fused kernel and return a fresh contiguous ``[B, S, H, D]`` tensor."""
+    """Run the fused kernel and return a fresh contiguous ``[B, S, H, D]`` tensor.
+
+    ``schedule`` ("auto", "two_pass", "one_pass") picks the softmax schedule
+    of 16-bit inputs on the tensor-core route: two passes round the
+    normalised probabilities to the input dtype (the explicit reference's
+    rounding); one pass rounds them before normalisation and does half the
+    exponentials and two thirds of the MMAs. fp32 has a single schedule."""
     support = b200_attention_support(q, k, v, valid_token_mask)
     if not support.supported:
         raise ValueError(f"unsupported b200 attention input: {support.reason}")
@@ -46,7 +53,7 @@ def b200_attention(
     if output.numel() == 0:
         return output
     with torch.cuda.device(q.device):
-        _native.attention_fwd(q, k, v, valid_token_mask, output, causal, softmax_scale)
+        _native.attention_fwd(q, k, v, valid_token_mask, output, causal, softmax_scale, schedule)
     return output
 
 
