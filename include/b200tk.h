@@ -186,6 +186,34 @@ B200TK_API int b200tk_linear_gelu_fwd(const void* x, const void* weight, const v
                                       int64_t out_features, void* stream);
 
 /*
+ * out_proj / ffn_out with the residual add that follows it fused into the
+ * GEMM epilogue:
+ *   out[m, n] = residual[m, n] + (sum_k x[m, k] * weight[n, k] + bias[n])
+ * and, when valid_rows is given, out[m, :] = 0 for every row m whose byte is 0
+ * (the block-end zeroing of padded rows).
+ *
+ * Replaces: the `x + layer.attention(...)` / `x + layer.ffn_out(...)` pairs of
+ * the reference's block (benchmarks/torch_transformer_benchmark.py:140-141),
+ * as placed by its fused layer loop at transformer_opt/submission.py:499-523
+ * (there: a cuBLAS GEMM writing the projection, then the residual-add kernel
+ * reading it back).
+ *
+ * x : [rows, in_features], weight : [out_features, in_features] (nn.Linear
+ * layout), residual and out : [rows, out_features], all row-major in `dtype`;
+ * bias : [out_features] or NULL; valid_rows : [rows] bytes or NULL. out may
+ * not alias x; it may alias residual. Accumulation and bias are fp32; the
+ * projection is rounded to dtype before the add (16-bit), as the unfused
+ * Linear's output tensor is, and the sum is rounded to dtype. float32
+ * multiplies as TF32 with truncated operands (see b200tk_linear_gelu_fwd).
+ * Alignment and size rules are those of b200tk_linear_gelu_fwd.
+ */
+B200TK_API int b200tk_linear_residual_fwd(const void* x, const void* weight, const void* bias,
+                                          const void* residual, const uint8_t* valid_rows,
+                                          void* out, int dtype, int64_t rows,
+                                          int64_t in_features, int64_t out_features,
+                                          void* stream);
+
+/*
  * Read (and, with clear != 0, reset) the device status word of `device`.
  * Synchronises the device. Not for use inside stream capture.
  */

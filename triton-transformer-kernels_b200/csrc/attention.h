@@ -74,20 +74,24 @@ struct RlnArgs {
 };
 cudaError_t launch_residual_layer_norm(const RlnArgs& args, cudaStream_t stream);
 
-// Linear + exact GELU (the FFN input projection). Tensor maps are built by
-// the host: x [rows, k_in], weight [n_out, k_in] and out [rows, n_out], all
-// row-major.
+// Linear + exact GELU (the FFN input projection) and Linear + residual add
+// (out_proj / ffn_out). Tensor maps are built by the host: x [rows, k_in],
+// weight [n_out, k_in] and out [rows, n_out], all row-major; residual
+// [rows, n_out] row-major and row_mask [rows] (residual form only).
 struct LinearGeluArgs {
   alignas(64) unsigned char tm_x[128];
   alignas(64) unsigned char tm_w[128];
   alignas(64) unsigned char tm_out[128];
   const void* bias;
+  const void* residual;
+  const uint8_t* row_mask;
   void* out;
   int64_t rows, k_in, n_out;
   int dtype;
   unsigned int* status;
 };
 cudaError_t launch_linear_gelu(const LinearGeluArgs& args, cudaStream_t stream);
+cudaError_t launch_linear_residual(const LinearGeluArgs& args, cudaStream_t stream);
 
 // Failure-detection self test (bounded wait on an mbarrier nobody completes).
 cudaError_t launch_selftest_wait_timeout(unsigned int* status, uint32_t timeout_us,

@@ -57,6 +57,7 @@ cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
   prm.scale_pow2 = a.dtype == B200TK_DTYPE_BFLOAT16 && a.scale > 0.f &&
                    std::frexp(a.scale, &exponent) == 0.5f;
   prm.one_pass = attention_tc_one_pass(a.dtype, a.seq, a.scale, a.schedule) ? 1 : 0;
+  prm.exact_exp = a.schedule == 3 ? 1 : 0;
   prm.status = a.status;
   const bool causal = a.causal != 0;
   const bool has_mask = a.mask != nullptr;

@@ -72,6 +72,7 @@ struct __align__(64) AttnTcParams {
   int causal_pairs;    // persistent causal schedule over (long, short) tile pairs
   int scale_pow2;      // bf16 only: scale is an exact power of two
   int one_pass;        // 16-bit only: online softmax (see TcLayout::kTwoPass)
+  int exact_exp;       // 16-bit two-pass: libm expf and IEEE division (experiment)
   unsigned int* status;
 };
 
@@ -282,11 +283,14 @@ struct TcLayout {
   static_assert(!kSplit || NQ == 1, "fp32 keeps one query tile per CTA");
 };
 
-template <typename T, int D, int BN, int KST, int VST, int NQ, bool OP, bool CAUSAL,
+// SCHED: 0 two-pass, 1 one-pass (16-bit), 2 two-pass with libm expf and IEEE
+// division (16-bit, experimental).
+template <typename T, int D, int BN, int KST, int VST, int NQ, int SCHED, bool CAUSAL,
           bool HAS_MASK>
-__global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads, 1)
+__global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>::kThreads, 1)
     attention_fwd_tc_kernel(const __grid_constant__ AttnTcParams p) {
-  using L = TcLayout<T, D, BN, KST, VST, NQ, OP>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>;
+  constexpr bool kExactExp = SCHED == 2;
   constexpr bool kSplit = L::kSplit;
   constexpr int NSB = L::kNSB;
   constexpr bool kTwoPass = L::kTwoPass;
@@ -836,6 +840,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads
         float m_run = -INFINITY;  // running max of this half, log2 units
         float l_run = 0.f;
         float m_fin = 0.f, inv_l = 0.f;  // row max (log2 units) and 1/row sum
+        float l_fin = 0.f;               // row sum
 
         for (int g = 0; g < w.n_s && ok; ++g) {
           const int sg = kc + g;
@@ -934,17 +939,28 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads
 
           if (!pass2) {
             // pass 1: running max and sum of this half
-            const float m_new = fmaxf(m_run, mx * kLog2e);
+            constexpr bool ex = kExactExp;
+            const float m_new = fmaxf(m_run, ex ? mx : mx * kLog2e);
             const float m_use = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_use);
+            const float alpha = m_run == -INFINITY ? 0.f
+                                : ex               ? expf(m_run - m_use)
+                                                   : ex2_approx(m_run - m_use);
             float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if constexpr (ex) {
 #pragma unroll
-            for (int i = 0; i < HB; i += 2) {
-              float a = sv[i], c = sv[i + 1];
-              fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
-              a = ex2_approx(a);
-              c = ex2_approx(c);
-              add2(part[i % 8], part[i % 8 + 1], a, c);
+              for (int i = 0; i < HB; i += 2) {
+                const float a = expf(sv[i] - m_use), c = expf(sv[i + 1] - m_use);
+                add2(part[i % 8], part[i % 8 + 1], a, c);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < HB; i += 2) {
+                float a = sv[i], c = sv[i + 1];
+                fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
+                a = ex2_approx(a);
+                c = ex2_approx(c);
+                add2(part[i % 8], part[i % 8 + 1], a, c);
+              }
             }
             add2(part[0], part[1], part[2], part[3]);
             add2(part[4], part[5], part[6], part[7]);
@@ -961,26 +977,40 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads
               const float2 other = stats[(t * 2 + (half ^ 1)) * BM + r];
               const float mm = fmaxf(m_run, other.x);
               const float mu = mm == -INFINITY ? 0.f : mm;
-              const float la = m_run == -INFINITY ? 0.f : l_run * ex2_approx(m_run - mu);
-              const float lb = other.x == -INFINITY ? 0.f : other.y * ex2_approx(other.x - mu);
+              const float la = m_run == -INFINITY ? 0.f
+                               : ex               ? l_run * expf(m_run - mu)
+                                                  : l_run * ex2_approx(m_run - mu);
+              const float lb = other.x == -INFINITY ? 0.f
+                               : ex                 ? other.y * expf(other.x - mu)
+                                                    : other.y * ex2_approx(other.x - mu);
               // same association on both threads of the row: (half 0) + (half 1)
               const float l = half == 0 ? la + lb : lb + la;
               m_fin = mu;
               inv_l = l > 0.f ? 1.f / l : 0.f;
+              l_fin = l;
             }
             continue;
           }
 
           // pass 2: normalised probabilities, rounded to T, into TMEM
           uint32_t pk[HB / 2];
+          if constexpr (kExactExp) {
 #pragma unroll
-          for (int i = 0; i < HB; i += 2) {
-            float a = sv[i], c = sv[i + 1];
-            fma2(a, c, kLog2e, kLog2e, -m_fin, -m_fin);
-            a = ex2_approx(a);
-            c = ex2_approx(c);
-            mul2(a, c, inv_l, inv_l);
-            pk[i / 2] = cvt_pack2<T>(a, c);
+            for (int i = 0; i < HB; i += 2) {
+              const float a = l_fin > 0.f ? __fdiv_rn(expf(sv[i] - m_fin), l_fin) : 0.f;
+              const float c = l_fin > 0.f ? __fdiv_rn(expf(sv[i + 1] - m_fin), l_fin) : 0.f;
+              pk[i / 2] = cvt_pack2<T>(a, c);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < HB; i += 2) {
+              float a = sv[i], c = sv[i + 1];
+              fma2(a, c, kLog2e, kLog2e, -m_fin, -m_fin);
+              a = ex2_approx(a);
+              c = ex2_approx(c);
+              mul2(a, c, inv_l, inv_l);
+              pk[i / 2] = cvt_pack2<T>(a, c);
+            }
           }
           if (j > 0) {
             // Waiting for every P@V phase in order keeps the pv_done parity
@@ -1487,11 +1517,11 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads
   }
 }
 
-template <typename T, int D, int BN, int KST, int VST, int NQ, bool OP, bool CAUSAL,
+template <typename T, int D, int BN, int KST, int VST, int NQ, int SCHED, bool CAUSAL,
           bool HAS_MASK>
 cudaError_t launch_tc(const AttnTcParams& prm, int grid, cudaStream_t stream) {
-  using L = TcLayout<T, D, BN, KST, VST, NQ, OP>;
-  auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, OP, CAUSAL, HAS_MASK>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>;
+  auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, SCHED, CAUSAL, HAS_MASK>;
   // at least ~116 KB so that one CTA (and one TMEM allocation) owns each SM
   const int smem = L::kBytes > 118 * 1024 ? L::kBytes : 118 * 1024;
   // The opt-in shared-memory size is set once per device and instantiation,
@@ -1528,7 +1558,7 @@ struct TcTile<float, 128> {
   static constexpr int kNQ = 1, kBN = 32, kKST = 2, kVST = 2;
 };
 
-template <typename T, int D, bool OP>
+template <typename T, int D, int OP>
 cudaError_t launch_variant(const AttnTcParams& prm, int grid, bool causal, bool has_mask,
                            cudaStream_t stream) {
   using C = TcTile<T, D>;
@@ -1569,9 +1599,10 @@ cudaError_t launch_dtype_hd(AttnTcParams prm, int num_sms, bool causal, bool has
   const bool persistent = !causal || prm.causal_pairs;
   const int grid = static_cast<int>(persistent ? (work < num_sms ? work : num_sms) : work);
   if constexpr (!std::is_same_v<T, float>) {
-    if (prm.one_pass) return launch_variant<T, D, true>(prm, grid, causal, has_mask, stream);
+    if (prm.one_pass) return launch_variant<T, D, 1>(prm, grid, causal, has_mask, stream);
+    if (prm.exact_exp) return launch_variant<T, D, 2>(prm, grid, causal, has_mask, stream);
   }
-  return launch_variant<T, D, false>(prm, grid, causal, has_mask, stream);
+  return launch_variant<T, D, 0>(prm, grid, causal, has_mask, stream);
 }
 
 // Explicit instantiations live in attention_tc_inst.cu, compiled once per

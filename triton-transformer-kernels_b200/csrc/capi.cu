@@ -263,7 +263,7 @@ int b200tk_attention_fwd_scheduled(const void* q, const int64_t* q_strides, cons
                                    int64_t head_dim, int causal, float scale, int schedule,
                                    void* stream) {
   if (schedule != B200TK_SCHEDULE_AUTO && schedule != B200TK_SCHEDULE_TWO_PASS &&
-      schedule != B200TK_SCHEDULE_ONE_PASS)
+      schedule != B200TK_SCHEDULE_ONE_PASS && schedule != 3)
     return fail(B200TK_ERR_INVALID_ARGUMENT, "unknown attention schedule");
   int rc = validate_attention(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len,
                               heads, head_dim);
@@ -410,6 +410,48 @@ int b200tk_linear_gelu_fwd(const void* x, const void* weight, const void* bias, 
   a.dtype = dtype;
   cudaError_t err = launch_linear_gelu(a, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "linear gelu launch");
+  return B200TK_OK;
+}
+
+int b200tk_linear_residual_fwd(const void* x, const void* weight, const void* bias,
+                               const void* residual, const uint8_t* valid_rows, void* out,
+                               int dtype, int64_t rows, int64_t in_features,
+                               int64_t out_features, void* stream) {
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(B200TK_ERR_INVALID_ARGUMENT, "unknown dtype code");
+  if (rows < 0 || in_features <= 0 || out_features <= 0)
+    return fail(B200TK_ERR_INVALID_ARGUMENT, "rows >= 0, in_features > 0 and out_features > 0");
+  if (rows > (int64_t(1) << 31) - 256 || out_features > (int64_t(1) << 30) ||
+      in_features > (int64_t(1) << 30))
+    return fail(B200TK_ERR_UNSUPPORTED, "matrix extent exceeds the kernel's index range");
+  if ((in_features * es) % 16 != 0 || (out_features * es) % 16 != 0)
+    return fail(B200TK_ERR_UNSUPPORTED,
+                "in_features and out_features must be multiples of 16 bytes of elements");
+  if (rows == 0) return B200TK_OK;
+  if (x == nullptr || weight == nullptr || residual == nullptr || out == nullptr)
+    return fail(B200TK_ERR_INVALID_ARGUMENT, "x, weight, residual and out must not be NULL");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(out) || !aligned16(residual) ||
+      (bias != nullptr && !aligned16(bias)))
+    return fail(B200TK_ERR_UNSUPPORTED,
+                "x, weight, bias, residual and out must be 16-byte aligned");
+  LinearGeluArgs a;
+  std::memset(&a, 0, sizeof(a));
+  int rc = encode_matrix_map(a.tm_x, x, rows, in_features, dtype, 128);
+  if (rc == B200TK_OK) rc = encode_matrix_map(a.tm_w, weight, out_features, in_features, dtype, 128);
+  if (rc == B200TK_OK) rc = encode_matrix_map(a.tm_out, out, rows, out_features, dtype, 32);
+  if (rc != B200TK_OK) return rc;
+  rc = status_address(&a.status);
+  if (rc != B200TK_OK) return rc;
+  a.bias = bias;
+  a.residual = residual;
+  a.row_mask = valid_rows;
+  a.out = out;
+  a.rows = rows;
+  a.k_in = in_features;
+  a.n_out = out_features;
+  a.dtype = dtype;
+  cudaError_t err = launch_linear_residual(a, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "linear residual launch");
   return B200TK_OK;
 }
 

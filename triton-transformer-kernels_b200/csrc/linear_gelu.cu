@@ -1,8 +1,19 @@
-// linear_gelu.cu - the FFN input projection with its activation fused into
-// the GEMM epilogue:
+// linear_gelu.cu - tcgen05 CTA-pair GEMMs of the Transformer block with
+// their elementwise consumers fused into the epilogue:
 //
-//   out[m, n] = gelu(sum_k x[m, k] * weight[n, k] + bias[n]),
-//   gelu(v)   = v * 0.5 * (1 + erf(v / sqrt(2)))        (exact, erf form)
+//   GELU     out[m, n] = gelu(sum_k x[m, k] * weight[n, k] + bias[n]),
+//            gelu(v)   = v * 0.5 * (1 + erf(v / sqrt(2)))   (exact, erf form)
+//   RESIDUAL out[m, n] = res[m, n] + (sum_k x[m, k] * weight[n, k] + bias[n])
+//            (rows whose row mask byte is 0 written as 0, when a mask is given)
+//
+// GELU is the FFN input projection; RESIDUAL is out_proj and ffn_out with the
+// residual add that follows each (`x + attn(norm1(x))`, `x + ffn(...)`,
+// benchmarks/torch_transformer_benchmark.py:140-141, placed by the fused
+// layer loop at transformer_opt/submission.py:499-523): the projection's
+// [rows, d] output is never written, and the residual stream is written once.
+// Rounding of RESIDUAL follows the unfused reference: fp32 accumulation plus
+// bias, rounded to T (the Linear's output tensor), added to the residual in
+// fp32 and rounded to T again (a single fp32 add for T = float).
 //
 // This is `F.gelu(layer.ffn_in(h), approximate="none")` of the reference's
 // block (benchmarks/torch_transformer_benchmark.py:131, 141; its fused layer
@@ -89,11 +100,17 @@ struct Layout {
   static_assert(kChunks % 2 == 0, "chunks are processed in pairs");
 };
 
+// Epilogue operations.
+constexpr int kEpiGelu = 0;
+constexpr int kEpiResidual = 1;
+
 struct __align__(64) LgParams {
   CUtensorMap tm_x;  // [rows, k] row-major, box {128 bytes, BM rows}
   CUtensorMap tm_w;  // [n, k] row-major, box {128 bytes, kHalfN rows}
   CUtensorMap tm_out;  // [rows, n] row-major, box {128 bytes, 32 rows}
   const void* bias;  // [n] or nullptr
+  const void* residual;     // RESIDUAL: [rows, n] row-major
+  const uint8_t* row_mask;  // RESIDUAL: [rows] or nullptr (0 -> output row 0)
   int64_t rows;
   int n_out;
   int m_tiles, n_tiles, k_blocks;
@@ -188,9 +205,37 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
+// The 32 residual elements of one row starting at column c0, as stored
+// (fp32: 32 words, 16-bit: 16 words of packed pairs); 16-byte pieces at or
+// past n_out read as zero (n_out is a multiple of 16 bytes of elements, so a
+// piece is wholly in or out).
 template <typename T>
-__global__ void __launch_bounds__(Layout<T>::kThreads, 1)
-    linear_gelu_kernel(const __grid_constant__ LgParams p) {
+__device__ __forceinline__ void load_residual32(const T* row, int c0, int n_out,
+                                                uint32_t (&w)[32 * sizeof(T) / 4]) {
+  constexpr int kVec = 16 / static_cast<int>(sizeof(T));  // elements per 16 bytes
+#pragma unroll
+  for (int u = 0; u < 32 / kVec; ++u) {
+    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    if (c0 + u * kVec < n_out) raw = __ldg(reinterpret_cast<const uint4*>(row + c0 + u * kVec));
+    w[4 * u] = raw.x, w[4 * u + 1] = raw.y, w[4 * u + 2] = raw.z, w[4 * u + 3] = raw.w;
+  }
+}
+
+// Element j of a row loaded by load_residual32, in fp32.
+template <typename T>
+__device__ __forceinline__ float residual_at(const uint32_t* w, int j) {
+  if constexpr (std::is_same_v<T, float>) {
+    return __uint_as_float(w[j]);
+  } else if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    return __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16));
+  } else {
+    const __half2 h = *reinterpret_cast<const __half2*>(&w[j >> 1]);
+    return (j & 1) ? __high2float(h) : __low2float(h);
+  }
+}
+
+template <typename T, int EPI>
+__device__ __forceinline__ void linear_tc_body(const LgParams& p) {
   using L = Layout<T>;
   constexpr int kStages = L::kStages;
   constexpr int kEpiWarps = L::kEpiWarps;
@@ -396,6 +441,7 @@ __global__ void __launch_bounds__(Layout<T>::kThreads, 1)
     const uint32_t srow = staging + lane * 128;  // this lane's staging row
     constexpr bool kWide = L::kWide;  // 32 outputs fill a staging row
     const T* bias = static_cast<const T*>(p.bias);
+    const T* residual = static_cast<const T*>(p.residual);
     if (lane == 0) tma_prefetch_desc(&p.tm_out);
     int tc = 0;
     for (int t = pair; t < total; t += npairs, ++tc) {
@@ -412,6 +458,11 @@ __global__ void __launch_bounds__(Layout<T>::kThreads, 1)
       if (!__all_sync(0xFFFFFFFFu, wait(bar_acc_full(buf), (tc >> 1) & 1))) break;
       tc_fence_after();
       const int row0 = m * 2 * BM + static_cast<int>(rank) * BM + quarter * 32;  // warp's first row
+      // RESIDUAL: this lane's row of the residual, and whether it is kept
+      const int64_t my_row = static_cast<int64_t>(row0) + lane;
+      const T* res_row = residual + my_row * p.n_out;
+      const bool row_in = my_row < p.rows;
+      const bool row_kept = p.row_mask == nullptr || (row_in && p.row_mask[my_row] != 0);
       // bias, rounding, GELU, staging and (when a staging row is full) the
       // store of the 32 columns held in r
       auto chunk = [&](const uint32_t(&r)[32], int c) {
@@ -422,8 +473,16 @@ __global__ void __launch_bounds__(Layout<T>::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xFFFFFFFFu, bl[j & 3], c * 8 + (j >> 2));
         }
+        if constexpr (EPI == kEpiGelu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_out<T>(round_to<T>(v[j]));
+          for (int j = 0; j < 32; ++j) v[j] = gelu_out<T>(round_to<T>(v[j]));
+        } else {
+          uint32_t res[32 * sizeof(T) / 4] = {};
+          if (row_in) load_residual32<T>(res_row, col0 + c * 32, p.n_out, res);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = row_kept ? round_to<T>(residual_at<T>(res, j) + round_to<T>(v[j])) : 0.f;
+        }
         // the staging tile is free once the previous store has read it
         if (kWide || (c & 1) == 0) {
           if (lane == 0) bulk_wait_read_all();
@@ -504,12 +563,24 @@ __global__ void __launch_bounds__(Layout<T>::kThreads, 1)
   }
 }
 
+template <typename T>
+__global__ void __launch_bounds__(Layout<T>::kThreads, 1)
+    linear_gelu_kernel(const __grid_constant__ LgParams p) {
+  linear_tc_body<T, kEpiGelu>(p);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(Layout<T>::kThreads, 1)
+    linear_residual_kernel(const __grid_constant__ LgParams p) {
+  linear_tc_body<T, kEpiResidual>(p);
+}
+
 // Resident CTA pairs for this instantiation on the current device (queried
 // once per device), and the one-time opt-in shared-memory attribute.
-template <typename T>
+template <typename T, int EPI>
 cudaError_t prepare(int device, int* pairs) {
   static std::atomic<int> cached[64] = {};
-  auto kernel = linear_gelu_kernel<T>;
+  auto kernel = EPI == kEpiGelu ? linear_gelu_kernel<T> : linear_residual_kernel<T>;
   int v = cached[device].load(std::memory_order_acquire);
   if (v == 0) {
     cudaError_t err =
@@ -538,10 +609,10 @@ cudaError_t prepare(int device, int* pairs) {
   return cudaSuccess;
 }
 
-template <typename T>
+template <typename T, int EPI>
 cudaError_t launch_typed(const LgParams& prm, int device, cudaStream_t stream) {
   int resident = 0;
-  cudaError_t err = prepare<T>(device, &resident);
+  cudaError_t err = prepare<T, EPI>(device, &resident);
   if (err != cudaSuccess) return err;
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
   const int pairs = static_cast<int>(tiles < resident ? tiles : resident);
@@ -557,19 +628,24 @@ cudaError_t launch_typed(const LgParams& prm, int device, cudaStream_t stream) {
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  err = cudaLaunchKernelEx(&cfg, linear_gelu_kernel<T>, prm);
+  err = cudaLaunchKernelEx(&cfg, EPI == kEpiGelu ? linear_gelu_kernel<T> : linear_residual_kernel<T>,
+                           prm);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 
 }  // namespace lg
 
-cudaError_t launch_linear_gelu(const LinearGeluArgs& a, cudaStream_t stream) {
+namespace {
+
+cudaError_t launch_linear(const LinearGeluArgs& a, int epi, cudaStream_t stream) {
   lg::LgParams prm;
   prm.tm_x = *reinterpret_cast<const CUtensorMap*>(a.tm_x);
   prm.tm_w = *reinterpret_cast<const CUtensorMap*>(a.tm_w);
   prm.tm_out = *reinterpret_cast<const CUtensorMap*>(a.tm_out);
   prm.bias = a.bias;
+  prm.residual = a.residual;
+  prm.row_mask = a.row_mask;
   prm.rows = a.rows;
   prm.n_out = static_cast<int>(a.n_out);
   const int es = a.dtype == B200TK_DTYPE_FLOAT32 ? 4 : 2;
@@ -585,12 +661,29 @@ cudaError_t launch_linear_gelu(const LinearGeluArgs& a, cudaStream_t stream) {
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  const bool gelu = epi == lg::kEpiGelu;
   switch (a.dtype) {
-    case B200TK_DTYPE_FLOAT32: return lg::launch_typed<float>(prm, device, stream);
-    case B200TK_DTYPE_FLOAT16: return lg::launch_typed<__half>(prm, device, stream);
-    case B200TK_DTYPE_BFLOAT16: return lg::launch_typed<__nv_bfloat16>(prm, device, stream);
+    case B200TK_DTYPE_FLOAT32:
+      return gelu ? lg::launch_typed<float, lg::kEpiGelu>(prm, device, stream)
+                  : lg::launch_typed<float, lg::kEpiResidual>(prm, device, stream);
+    case B200TK_DTYPE_FLOAT16:
+      return gelu ? lg::launch_typed<__half, lg::kEpiGelu>(prm, device, stream)
+                  : lg::launch_typed<__half, lg::kEpiResidual>(prm, device, stream);
+    case B200TK_DTYPE_BFLOAT16:
+      return gelu ? lg::launch_typed<__nv_bfloat16, lg::kEpiGelu>(prm, device, stream)
+                  : lg::launch_typed<__nv_bfloat16, lg::kEpiResidual>(prm, device, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+}  // namespace
+
+cudaError_t launch_linear_gelu(const LinearGeluArgs& a, cudaStream_t stream) {
+  return launch_linear(a, lg::kEpiGelu, stream);
+}
+
+cudaError_t launch_linear_residual(const LinearGeluArgs& a, cudaStream_t stream) {
+  return launch_linear(a, lg::kEpiResidual, stream);
 }
 
 }  // namespace b200tk

@@ -33,7 +33,7 @@ RLN_ROUND_TF32 = 8
 STATUS_PIPELINE_TIMEOUT = 1
 STATUS_SELFTEST_TIMEOUT = 2
 
-SCHEDULES = {"auto": 0, "two_pass": 1, "one_pass": 2}
+SCHEDULES = {"auto": 0, "two_pass": 1, "one_pass": 2, "exact_exp": 3}
 
 ROUTE_TCGEN05 = 1
 ROUTE_GENERIC = 2
@@ -62,6 +62,7 @@ SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, ctypes.c_float, ctypes.c_uint32, _P],
     ),
     "b200tk_linear_gelu_fwd": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
+    "b200tk_linear_residual_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
     "b200tk_device_status": (_I, [_I, ctypes.POINTER(ctypes.c_uint32), _I]),
     "b200tk_selftest_wait_timeout": (_I, [_I, ctypes.c_uint32, _P]),
 }
@@ -224,6 +225,31 @@ def linear_gelu_fwd(
     rc = lib.b200tk_linear_gelu_fwd(
         ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(weight.data_ptr()),
         None if bias is None else ctypes.c_void_p(bias.data_ptr()),
+        ctypes.c_void_p(out.data_ptr()),
+        DTYPE_CODES[x.dtype], rows, in_features, weight.shape[0],
+        _stream_handle(x.device),
+    )
+    _check(rc)
+
+
+def linear_residual_fwd(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: Optional[torch.Tensor],
+    residual: torch.Tensor,
+    valid_rows: Optional[torch.Tensor],
+    out: torch.Tensor,
+) -> None:
+    """Launch out = residual + (x @ weight.T + bias) (rows zeroed where
+    valid_rows is False) on the current stream of x's device."""
+    lib = load()
+    in_features = x.shape[-1]
+    rows = x.numel() // in_features if in_features else 0
+    rc = lib.b200tk_linear_residual_fwd(
+        ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(weight.data_ptr()),
+        None if bias is None else ctypes.c_void_p(bias.data_ptr()),
+        ctypes.c_void_p(residual.data_ptr()),
+        None if valid_rows is None else ctypes.c_void_p(valid_rows.data_ptr()),
         ctypes.c_void_p(out.data_ptr()),
         DTYPE_CODES[x.dtype], rows, in_features, weight.shape[0],
         _stream_handle(x.device),

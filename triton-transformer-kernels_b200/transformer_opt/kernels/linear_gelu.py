@@ -1,4 +1,6 @@
-"""FFN input projection with its exact GELU fused on sm_100a (libb200tk.so).
+"""Block GEMMs with their elementwise consumers fused on sm_100a (libb200tk.so):
+the FFN input projection with its exact GELU, and out_proj / ffn_out with the
+residual add that follows them.
 
 ``fused_linear_gelu(x, weight, bias)`` computes
 ``F.gelu(F.linear(x, weight, bias), approximate="none")`` -- the
@@ -89,4 +91,42 @@ def fused_linear_gelu(
     if x.numel() == 0:
         return out
     _native.linear_gelu_fwd(x, weight, bias, out)
+    return out
+
+
+def fused_linear_residual(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: Optional[torch.Tensor],
+    residual: torch.Tensor,
+    valid_rows: Optional[torch.Tensor] = None,
+    *,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """``residual + F.linear(x, weight, bias)`` as one GEMM whose epilogue adds
+    the residual (the projection rounded to x's dtype first, as the unfused
+    Linear's output tensor is); rows where ``valid_rows`` is False are
+    written as zeros. ``out`` may be ``residual`` itself (in place)."""
+    reason = linear_gelu_unsupported_reason(x, weight, bias)
+    if reason is not None:
+        raise ValueError(reason)
+    shape = (*x.shape[:-1], weight.shape[0])
+    if residual.shape != shape or residual.dtype != x.dtype or residual.device != x.device or (
+        not residual.is_contiguous() or residual.data_ptr() % 16
+    ):
+        raise ValueError("residual must be a contiguous, 16-byte aligned tensor of the output shape")
+    if valid_rows is not None and (
+        valid_rows.shape != shape[:-1] or valid_rows.dtype is not torch.bool
+        or valid_rows.device != x.device or not valid_rows.is_contiguous()
+    ):
+        raise ValueError("valid_rows must be a contiguous bool tensor of the row shape on x's device")
+    if out is None:
+        out = torch.empty(shape, dtype=x.dtype, device=x.device)
+    elif out.shape != shape or out.dtype != x.dtype or out.device != x.device or (
+        not out.is_contiguous() or out.data_ptr() % 16
+    ):
+        raise ValueError("out must be a contiguous, 16-byte aligned tensor of the output shape")
+    if x.numel() == 0:
+        return out
+    _native.linear_residual_fwd(x, weight, bias, residual, valid_rows, out)
     return out
