@@ -243,3 +243,40 @@ def test_baseline_config_shapes_full_size(name):
         ref = oracle.reference_attention_rows(q[bsel], k[bsel], v[bsel], rows, None, causal)
     assert_within_contract(out[bsel][:, rows], ref)
     assert torch.isfinite(out).all()
+
+
+def test_schedule_routing_by_sequence_length():
+    # "auto": two passes (normalised probabilities rounded to the dtype, the
+    # explicit math's rounding) below 4096 keys, one online pass from 4096 on
+    from transformer_opt.kernels.attention import b200_attention
+
+    torch.manual_seed(61)
+    for seq, expected in ((1000, "two_pass"), (4096, "one_pass")):
+        q = (torch.randn(1, seq, 2, 128, device="cuda") * 128 ** -0.5).to(torch.bfloat16)
+        k, v = torch.randn_like(q), torch.randn_like(q)
+        with torch.inference_mode():
+            auto = b200_attention(q, k, v, causal=True)
+            forced = b200_attention(q, k, v, causal=True, schedule=expected)
+        assert torch.equal(auto, forced)
+    q32 = torch.randn(1, 4096, 2, 64, device="cuda")  # fp32: one schedule only
+    with torch.inference_mode():
+        assert torch.equal(b200_attention(q32, q32, q32, schedule="one_pass"),
+                           b200_attention(q32, q32, q32, schedule="two_pass"))
+
+
+def test_c3_attention_meets_the_rule_on_every_element_five_seeds():
+    # C3's attention (bf16, causal, S=16384, 32 heads, head_dim 128; q, k, v
+    # ~ N(0,1) / sqrt(128)) on the schedule "auto" picks there (one pass),
+    # every query row of every batch element against the explicit math.
+    b, s, h, d = FULL["C3"][:4]
+    for seed in range(5):
+        g = torch.Generator(device="cuda").manual_seed(100 + seed)
+        q, k, v = ((torch.randn(b, s, h, d, device="cuda", generator=g) * d ** -0.5)
+                   .to(torch.bfloat16) for _ in range(3))
+        out = run_b200(q, k, v, causal=True)
+        for i in range(b):
+            with torch.inference_mode():
+                ref = oracle.reference_attention(q[i:i + 1], k[i:i + 1], v[i:i + 1], None, True)
+            assert_within_contract(out[i:i + 1], ref)
+            del ref
+            torch.cuda.empty_cache()

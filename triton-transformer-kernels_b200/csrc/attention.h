@@ -33,7 +33,7 @@ struct AttnTcArgs {
 int attention_tc_block_n(int dtype, int head_dim);
 // Sequence length from which B200TK_SCHEDULE_AUTO runs 16-bit inputs on the
 // one-pass schedule; shorter sequences keep the two-pass schedule.
-constexpr int64_t kOnePassMinSeq = int64_t(1) << 62;
+constexpr int64_t kOnePassMinSeq = 4096;
 // Whether a 16-bit tcgen05 launch takes the one-pass schedule.
 bool attention_tc_one_pass(int dtype, int64_t seq, float scale, int schedule);
 // Whether the tcgen05 kernel's work-item numbering fits in int for this

@@ -148,6 +148,36 @@ __device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
       : "f"(b0), "f"(b1));
 }
 
+// 2^x and 2^y for finite x, y <= 0 on the FMA and integer pipes instead of
+// the MUFU: Cody-Waite range reduction x = n + f with n = rint(x) (adding
+// 1.5 * 2^23 leaves n in the low mantissa bits) and f in [-1/2, 1/2], 2^f by a
+// degree-5 polynomial (coefficients fitted for this library by weighted least
+// squares on the relative error over [-1/2, 1/2]: max relative error 3.5e-7,
+// close to the hardware ex2.approx), and 2^n added to the exponent field.
+// Arguments are clamped at -126 (a result below 2^-126 is flushed to zero
+// by the hardware path; here it is at most 2^-126, far below the rounding of
+// any probability that is added to a row sum of at least 1).
+__device__ __forceinline__ void exp2_fma2(float& x, float& y) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  x = fmaxf(x, -126.0f);
+  y = fmaxf(y, -126.0f);
+  float tx = x, ty = y;
+  add2(tx, ty, kShift, kShift);         // rint(x) + shift
+  float nx = tx, ny = ty;
+  add2(nx, ny, -kShift, -kShift);       // rint(x)
+  float fx = x, fy = y;
+  add2(fx, fy, -nx, -ny);               // f = x - rint(x)
+  float px = 1.2915670e-3f, py = 1.2915670e-3f;
+  fma2(px, py, fx, fy, 9.6685309e-3f, 9.6685309e-3f);
+  fma2(px, py, fx, fy, 5.5516887e-2f, 5.5516887e-2f);
+  fma2(px, py, fx, fy, 2.4022265e-1f, 2.4022265e-1f);
+  fma2(px, py, fx, fy, 6.9314647e-1f, 6.9314647e-1f);
+  fma2(px, py, fx, fy, 1.0f, 1.0f);
+  // the integer part sits in the low bits of t: add it to the exponent
+  x = __uint_as_float(__float_as_uint(px) + ((__float_as_uint(tx) - 0x4B400000u) << 23));
+  y = __uint_as_float(__float_as_uint(py) + ((__float_as_uint(ty) - 0x4B400000u) << 23));
+}
+
 // Round two fp32 values to T and pack them (a in the low half).
 template <typename T>
 __device__ __forceinline__ uint32_t cvt_pack2(float a, float b) {
@@ -287,10 +317,14 @@ struct TcLayout {
 // division (16-bit, experimental).
 template <typename T, int D, int BN, int KST, int VST, int NQ, int SCHED, bool CAUSAL,
           bool HAS_MASK>
-__global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>::kThreads, 1)
+__global__ void __launch_bounds__(
+    TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1 || SCHED >= 3>::kThreads, 1)
     attention_fwd_tc_kernel(const __grid_constant__ AttnTcParams p) {
-  using L = TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1 || SCHED >= 3>;
   constexpr bool kExactExp = SCHED == 2;
+  // one-pass: every kPolyEvery-th probability pair of an unmasked tile is
+  // exponentiated on the FMA pipe (exp2_fma2) instead of the MUFU (0: none)
+  constexpr int kPolyEvery = SCHED == 3 ? 4 : SCHED == 4 ? 2 : 0;
   constexpr bool kSplit = L::kSplit;
   constexpr int NSB = L::kNSB;
   constexpr bool kTwoPass = L::kTwoPass;
@@ -1129,6 +1163,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>::
           tc_fence_after();
           const int n0 = j * BN;
           uint32_t pk[NP];  // T(qk) pairs; pair i belongs to row ra + 8 * (i & 1)
+          bool tile_masked;
           {
             uint32_t raw[NE];
             tmem_ld16x256b<8>(tmem + lane_off + L::t_s(t, buf), raw);
@@ -1149,8 +1184,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>::
 #pragma unroll
               for (int wd = 0; wd < BN / 32; ++wd) pad = pad || kbits[wd] != 0xFFFFFFFFu;
             }
-            const bool masked = pad || (n0 + BN > p.seq) || (CAUSAL && n0 + BN - 1 > row0 + rb);
-            if (masked) {
+            tile_masked = pad || (n0 + BN > p.seq) || (CAUSAL && n0 + BN - 1 > row0 + rb);
+            if (tile_masked) {
 #pragma unroll
               for (int e = 0; e < NE; ++e) {
                 const int c = e_col(e);
@@ -1237,8 +1272,12 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>::
               round_pair<T>(a, c);
               fma2(a, c, kLog2e, kLog2e, -m_use[h], -m_use[h]);
             }
-            a = ex2_approx(a);
-            c = ex2_approx(c);
+            if (kPolyEvery > 0 && i % kPolyEvery == kPolyEvery - 1 && !tile_masked) {
+              exp2_fma2(a, c);
+            } else {
+              a = ex2_approx(a);
+              c = ex2_approx(c);
+            }
             add2(part[h][0], part[h][1], a, c);
             pk[i] = cvt_pack2<T>(a, c);
           }
@@ -1520,7 +1559,7 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>::
 template <typename T, int D, int BN, int KST, int VST, int NQ, int SCHED, bool CAUSAL,
           bool HAS_MASK>
 cudaError_t launch_tc(const AttnTcParams& prm, int grid, cudaStream_t stream) {
-  using L = TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1 || SCHED >= 3>;
   auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, SCHED, CAUSAL, HAS_MASK>;
   // at least ~116 KB so that one CTA (and one TMEM allocation) owns each SM
   const int smem = L::kBytes > 118 * 1024 ? L::kBytes : 118 * 1024;
@@ -1599,6 +1638,8 @@ cudaError_t launch_dtype_hd(AttnTcParams prm, int num_sms, bool causal, bool has
   const bool persistent = !causal || prm.causal_pairs;
   const int grid = static_cast<int>(persistent ? (work < num_sms ? work : num_sms) : work);
   if constexpr (!std::is_same_v<T, float>) {
+    if (prm.one_pass == 3) return launch_variant<T, D, 3>(prm, grid, causal, has_mask, stream);
+    if (prm.one_pass == 4) return launch_variant<T, D, 4>(prm, grid, causal, has_mask, stream);
     if (prm.one_pass) return launch_variant<T, D, 1>(prm, grid, causal, has_mask, stream);
     if (prm.exact_exp) return launch_variant<T, D, 2>(prm, grid, causal, has_mask, stream);
   }

@@ -4,7 +4,8 @@
 // transformer_opt/kernels/residual_layer_norm.py:73-126):
 //   r = x + update                       rounded to the I/O dtype
 //   r = 0            where the row is invalid and ZERO_INVALID_RESIDUAL
-//   mean = sum(r) / width; var = sum((r - mean)^2) / width   (fp32, two-pass)
+//   mean, var of r in fp32 (Welford in ATen's order on the Welford path,
+//                    two passes over the register-resident row otherwise)
 //   n = (r - mean) * rsqrt(var + eps) * weight + bias
 //   n = 0            where the row is invalid and ZERO_INVALID_NORMALIZED
 //   n = tf32(n)      with ROUND_TF32 (float32): nearest TF32 value, ties away
@@ -13,6 +14,10 @@
 // HBM sees exactly one read of x, update and one write of r, n (the roofline
 // minimum of 4 * width * sizeof(T) bytes per row).
 //
+// Welford path (rows of whole 4-element groups up to 4096 wide): the
+// statistics in the order of ATen's vectorised LayerNorm kernel, so the
+// normalized output equals torch's layer_norm bit for bit (see
+// rln_welford_kernel).
 // Vector path: each thread holds VPT 16-byte vectors of the row; TPR threads
 // share a row (TPR <= 32: a warp segment reduced with shuffles; TPR > 32: whole
 // warps reduced through shared memory). Rows that are not a whole number of
@@ -273,6 +278,205 @@ __global__ void __launch_bounds__(256) rln_scalar_kernel(const RlnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Welford path: the row statistics in the order of ATen's vectorised
+// LayerNorm (PyTorch, aten/src/ATen/native/cuda/layer_norm_kernel.cu,
+// BSD-licensed), so that `normalized_out` equals torch.nn.functional.layer_norm
+// of the residual bit for bit. 16-bit models are sensitive to this: a
+// LayerNorm whose fp32 statistics round differently moves ~1 in 10^3 of its
+// 16-bit outputs by one unit, and downstream of attention that difference
+// survives to the model output (measured on the BASELINE configurations).
+//
+// Order: 128 threads per row; thread t takes the 4-element groups t, t + 128,
+// ... and folds their elements, in order, into a running (mean, m2, count)
+// with Welford's update (mean += delta / count, m2 += delta * (v - mean));
+// the 32 lanes of a warp then fold in the state of lane + 16, + 8, ..., + 1
+// (Chan's pairwise combination); warps 2 and 3 are folded into warps 0 and 1,
+// then warp 1 into warp 0. var = m2 / width, rstd = rsqrtf(var + eps),
+// n = weight * (rstd * (r - mean)) + bias. Every fused multiply-add that the
+// ordering depends on is spelled out with the _rn intrinsics.
+struct WelfordState {
+  float mean, m2, count;
+};
+
+__device__ __forceinline__ WelfordState welford_add(WelfordState s, float v, float inv_count) {
+  const float delta = __fsub_rn(v, s.mean);
+  const float mean = __fmaf_rn(delta, inv_count, s.mean);
+  return {mean, __fmaf_rn(delta, __fsub_rn(v, mean), s.m2), __fadd_rn(s.count, 1.f)};
+}
+
+// own (b) folded with other (a)
+__device__ __forceinline__ WelfordState welford_combine(WelfordState b, WelfordState a) {
+  const float count = __fadd_rn(a.count, b.count);
+  if (!(count > 0.f)) return {0.f, 0.f, count};
+  const float delta = __fsub_rn(b.mean, a.mean);
+  const float coef = __frcp_rn(count);
+  const float na = __fmul_rn(a.count, coef), nb = __fmul_rn(b.count, coef);
+  const float mean = __fmaf_rn(na, a.mean, __fmul_rn(nb, b.mean));
+  const float m2 = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), a.count), nb, __fadd_rn(a.m2, b.m2));
+  return {mean, m2, count};
+}
+
+template <typename T>
+struct Quad {  // 4 consecutive elements: 16 bytes (fp32) or 8 bytes (16-bit)
+  using Raw = std::conditional_t<std::is_same_v<T, float>, uint4, uint2>;
+  __device__ __forceinline__ static void unpack(const Raw& v, float (&f)[4]) {
+    if constexpr (std::is_same_v<T, float>) {
+      f[0] = __uint_as_float(v.x), f[1] = __uint_as_float(v.y);
+      f[2] = __uint_as_float(v.z), f[3] = __uint_as_float(v.w);
+    } else {
+      const uint32_t w[2] = {v.x, v.y};
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+          f[2 * i] = __uint_as_float(w[i] << 16);
+          f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        } else {
+          const float2 ff = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+          f[2 * i] = ff.x, f[2 * i + 1] = ff.y;
+        }
+      }
+    }
+  }
+  __device__ __forceinline__ static Raw pack(const float (&f)[4]) {
+    Raw v;
+    if constexpr (std::is_same_v<T, float>) {
+      v.x = __float_as_uint(f[0]), v.y = __float_as_uint(f[1]);
+      v.z = __float_as_uint(f[2]), v.w = __float_as_uint(f[3]);
+    } else {
+      uint32_t w[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+          w[i] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+          w[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      v.x = w[0], v.y = w[1];
+    }
+    return v;
+  }
+};
+
+constexpr int kWelfordThreads = 128;  // threads per row (4 warps)
+
+template <typename T, int NQ>  // NQ: 4-element groups per thread (width <= 512 * NQ)
+__global__ void __launch_bounds__(kWelfordThreads) rln_welford_kernel(const RlnArgs a) {
+  using Q = Quad<T>;
+  using Raw = typename Q::Raw;
+  __shared__ float xch[8];
+  const int t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const int64_t row = blockIdx.x;
+  const int n_quads = static_cast<int>(a.width / 4);
+  const bool has_update = !(a.flags & B200TK_RLN_NO_UPDATE);
+  bool valid = true;
+  if (a.mask != nullptr) valid = a.mask[row] != 0;
+  const bool zero_res = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_RESIDUAL);
+  const bool zero_norm = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_NORMALIZED);
+  const bool tf32 = std::is_same_v<T, float> && (a.flags & B200TK_RLN_ROUND_TF32);
+  const Raw* xq = reinterpret_cast<const Raw*>(static_cast<const T*>(a.x) + row * a.width);
+  const Raw* uq = reinterpret_cast<const Raw*>(static_cast<const T*>(a.update) + row * a.width);
+  Raw* rq = reinterpret_cast<Raw*>(static_cast<T*>(a.residual_out) + row * a.width);
+  Raw* nq = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + row * a.width);
+
+  Raw xr[NQ], ur[NQ];
+#pragma unroll
+  for (int i = 0; i < NQ; ++i) {
+    const int qi = i * kWelfordThreads + t;
+    const bool in = qi < n_quads;
+    xr[i] = in ? xq[qi] : Raw{};
+    ur[i] = (in && has_update) ? uq[qi] : Raw{};
+  }
+  float r[NQ][4];
+  WelfordState st{0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < NQ; ++i) {
+    const int qi = i * kWelfordThreads + t;
+    if (qi >= n_quads) break;  // later groups of this thread are past the row too
+    float fx[4], fu[4];
+    Q::unpack(xr[i], fx);
+    Q::unpack(ur[i], fu);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float v = has_update ? fx[e] + fu[e] : fx[e];
+      if constexpr (!std::is_same_v<T, float>) v = round_t<T>(v);
+      r[i][e] = zero_res ? 0.f : v;
+      // the count before this element is 4 * i + e: 1 / (4 * i + e + 1) folds
+      // to a correctly rounded constant
+      st = welford_add(st, r[i][e], 1.f / static_cast<float>(4 * i + e + 1));
+    }
+    if (has_update) rq[qi] = Q::pack(r[i]);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const WelfordState o{__shfl_down_sync(0xFFFFFFFFu, st.mean, off),
+                         __shfl_down_sync(0xFFFFFFFFu, st.m2, off),
+                         __shfl_down_sync(0xFFFFFFFFu, st.count, off)};
+    st = welford_combine(st, o);
+  }
+  // warps 2, 3 -> 0, 1; then 1 -> 0 (lane 0 of each warp holds its state)
+#pragma unroll
+  for (int off = 2; off > 0; off >>= 1) {
+    if (lane == 0 && warp >= off && warp < 2 * off) {
+      xch[3 * (warp - off)] = st.mean;
+      xch[3 * (warp - off) + 1] = st.m2;
+      xch[3 * (warp - off) + 2] = st.count;
+    }
+    __syncthreads();
+    if (lane == 0 && warp < off)
+      st = welford_combine(st, WelfordState{xch[3 * warp], xch[3 * warp + 1], xch[3 * warp + 2]});
+    __syncthreads();
+  }
+  if (t == 0) {
+    xch[6] = st.mean;
+    xch[7] = __fdiv_rn(st.m2, static_cast<float>(a.width));
+  }
+  __syncthreads();
+  const float mean = xch[6];
+  const float rstd = rsqrtf(__fadd_rn(xch[7], a.eps));
+  const Raw* wq = static_cast<const Raw*>(a.weight);
+  const Raw* bq = static_cast<const Raw*>(a.bias);
+#pragma unroll
+  for (int i = 0; i < NQ; ++i) {
+    const int qi = i * kWelfordThreads + t;
+    if (qi >= n_quads) break;
+    float fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f}, o[4];
+    Q::unpack(wq[qi], fw);
+    if (bq != nullptr) Q::unpack(bq[qi], fb);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float c = __fmul_rn(rstd, __fsub_rn(r[i][e], mean));
+      const float nrm = bq != nullptr ? __fmaf_rn(fw[e], c, fb[e]) : __fmul_rn(fw[e], c);
+      o[e] = zero_norm ? 0.f : (tf32 ? round_tf32(nrm) : nrm);
+    }
+    nq[qi] = Q::pack(o);
+  }
+}
+
+template <typename T>
+cudaError_t launch_welford(const RlnArgs& a, cudaStream_t stream) {
+  const int64_t quads = a.width / 4;
+  const int nq = static_cast<int>((quads + kWelfordThreads - 1) / kWelfordThreads);
+  if (a.rows > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
+  const unsigned grid = static_cast<unsigned>(a.rows);
+  switch (nq) {
+    case 1: rln_welford_kernel<T, 1><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+    case 2: rln_welford_kernel<T, 2><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+    case 3: rln_welford_kernel<T, 3><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+    case 4: rln_welford_kernel<T, 4><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+    case 5: rln_welford_kernel<T, 5><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+    case 6: rln_welford_kernel<T, 6><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+    case 7: rln_welford_kernel<T, 7><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+    case 8: rln_welford_kernel<T, 8><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 template <typename T, int VPT, int TPR>
 cudaError_t launch_vec(const RlnArgs& a, cudaStream_t stream) {
   constexpr int kBlock = TPR >= 256 ? TPR : 256;
@@ -349,6 +553,14 @@ template <typename T>
 cudaError_t launch_typed(const RlnArgs& a, cudaStream_t stream) {
   constexpr int EPV = VecIO<T>::kEPV;
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  // Rows of whole 4-element groups, up to 4096 wide, take the Welford path
+  // (statistics in ATen's order); wider or unaligned rows the paths below.
+  const bool welford_ok = a.width % 4 == 0 && a.width <= 4 * kWelfordThreads * 8 &&
+                          aligned(a.x) && aligned(a.weight) && aligned(a.normalized_out) &&
+                          (a.bias == nullptr || aligned(a.bias)) &&
+                          ((a.flags & B200TK_RLN_NO_UPDATE) ||
+                           (aligned(a.update) && aligned(a.residual_out)));
+  if (welford_ok) return launch_welford<T>(a, stream);
   const bool vec_ok = a.width % EPV == 0 && aligned(a.x) && aligned(a.weight) &&
                       aligned(a.normalized_out) && (a.bias == nullptr || aligned(a.bias)) &&
                       ((a.flags & B200TK_RLN_NO_UPDATE) ||

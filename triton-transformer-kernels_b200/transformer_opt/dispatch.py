@@ -118,8 +118,14 @@ def attention_forward(
     causal: bool = False,
     scale: Optional[float] = None,
     backend: str = "auto",
+    schedule: str = "auto",
 ) -> Tuple[torch.Tensor, AttentionDispatch]:
-    """Execute attention and return both the output and the dispatch record."""
+    """Execute attention and return both the output and the dispatch record.
+
+    ``schedule`` (not in the reference's signature) picks the softmax
+    schedule of 16-bit inputs on the custom route: "two_pass" rounds
+    normalised probabilities (the explicit math's rounding), "one_pass" is
+    the online softmax, "auto" takes one pass from 4096 keys on."""
     _validate_backend(backend)
     support = b200_attention_support(q, k, v, valid_token_mask)
 
@@ -131,13 +137,17 @@ def attention_forward(
             raise RuntimeError(f"custom attention was forced but is unavailable: {detail}")
         if not support.supported:
             raise ValueError(f"custom attention was forced but unsupported: {support.reason}")
-        output = b200_attention(q, k, v, valid_token_mask, causal=causal, scale=scale)
+        output = b200_attention(
+            q, k, v, valid_token_mask, causal=causal, scale=scale, schedule=schedule
+        )
         return output, AttentionDispatch(backend, CUSTOM_BACKEND, support.reason)
 
     if backend == "auto" and support.supported:
         # Inside the envelope the kernel is the only route: a missing library
         # is an error here, never a silent downgrade.
-        output = b200_attention(q, k, v, valid_token_mask, causal=causal, scale=scale)
+        output = b200_attention(
+            q, k, v, valid_token_mask, causal=causal, scale=scale, schedule=schedule
+        )
         return output, AttentionDispatch("auto", CUSTOM_BACKEND, support.reason)
 
     if backend == "sdpa":

@@ -119,17 +119,33 @@ def layer_norm(
     weight: torch.Tensor,
     bias: Optional[torch.Tensor],
     eps: float,
+    valid_token_mask: Optional[torch.Tensor] = None,
+    *,
+    zero_invalid_normalized: bool = False,
+    round_normalized_tf32: bool = False,
 ) -> torch.Tensor:
-    """Plain LayerNorm over the last dimension through the same kernel."""
+    """Plain LayerNorm over the last dimension through the same kernel
+    (optionally zeroing invalid rows, or rounding the output to TF32 for
+    float32, as in ``fused_residual_layer_norm``)."""
     _check_input(x)
     if torch.is_grad_enabled() and x.requires_grad:
         raise ValueError("fused LayerNorm is forward-inference only")
     _check_affine(x, weight, bias)
+    if zero_invalid_normalized and valid_token_mask is None:
+        raise ValueError("invalid-row zeroing requires valid_token_mask")
+    _check_mask(x, valid_token_mask)
     _native.load()
     out = torch.empty_like(x)
+    flags = _native.RLN_NO_UPDATE
+    if zero_invalid_normalized:
+        flags |= _native.RLN_ZERO_INVALID_NORMALIZED
+    if round_normalized_tf32:
+        if x.dtype != torch.float32:
+            raise ValueError("TF32 rounding applies to float32 only")
+        flags |= _native.RLN_ROUND_TF32
     if x.numel():
         with torch.cuda.device(x.device):
             _native.residual_layer_norm_fwd(
-                x, None, weight, bias, None, None, out, eps, _native.RLN_NO_UPDATE
+                x, None, weight, bias, valid_token_mask, None, out, eps, flags
             )
     return out

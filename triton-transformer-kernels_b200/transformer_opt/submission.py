@@ -14,18 +14,25 @@ a replay never alias one another (the reference's contract for its graph
 path, submission.py:674-723). Up to GRAPH_CACHE_SIZE captures are kept.
 
 On an sm_100 GPU in inference mode every layer runs
-  packed QKV projection (cuBLAS, fp32) or three projections (16-bit)
-  -> fused attention (libb200tk, tcgen05)  -> out_proj (cuBLAS)
-  -> fused residual + norm2 (libb200tk)
+  packed QKV projection (cuBLAS, one GEMM)
+  -> fused attention (libb200tk, tcgen05)
+  -> out_proj + residual (16-bit: libb200tk, one tcgen05 GEMM with the
+     residual add in its epilogue, then LayerNorm norm2; fp32: cuBLAS, then
+     the fused residual + norm2 kernel)
   -> ffn_in + exact GELU (libb200tk, one tcgen05 GEMM with the GELU in its
-     epilogue)                              -> ffn_out (cuBLAS)
-  -> fused residual + next norm1 / final_norm (libb200tk)
+     epilogue)
+  -> ffn_out + residual + next norm1 / final_norm (as for out_proj)
 which is the reference's fused layer loop (:481-525) applied to every shape
 and dtype instead of four measured rows. ffn_backend ("auto" | "b200" |
 "torch") picks the FFN input projection: the fused kernel ("auto": where it
 applies and the output has at least FUSED_FFN_MIN_OUTPUTS elements; fp32
 only while TF32 matmuls are allowed, the precision the unfused fp32 Linear
-then has), or cuBLAS + ATen GELU. Everything else (CPU, autograd,
+then has), or cuBLAS + ATen GELU. residual_backend (same values) picks
+out_proj / ffn_out: GEMMs with the residual add in their epilogue followed
+by plain LayerNorms ("auto": 16-bit models), or cuBLAS + the fused residual
+LayerNorm. attention_schedule ("auto" | "two_pass" | "one_pass") is the
+16-bit softmax schedule of the attention kernel (see attention_forward).
+Everything else (CPU, autograd,
 training mode, backends other than the custom one) runs the explicit
 PyTorch forward with attention through ``attention_forward``.
 
@@ -58,7 +65,11 @@ from transformer_opt.config import (
 )
 from transformer_opt.dispatch import attention_forward
 from transformer_opt.kernels import _native
-from transformer_opt.kernels.linear_gelu import fused_linear_gelu, linear_gelu_unsupported_reason
+from transformer_opt.kernels.linear_gelu import (
+    fused_linear_gelu,
+    fused_linear_residual,
+    linear_gelu_unsupported_reason,
+)
 from transformer_opt.kernels.residual_layer_norm import fused_residual_layer_norm, layer_norm
 from transformer_opt.model import (
     SelfAttentionWeights,
@@ -70,6 +81,8 @@ from transformer_opt.model import (
 
 EXECUTION_MODES = ("auto", "eager", "graph")
 FFN_BACKENDS = ("auto", "b200", "torch")
+RESIDUAL_BACKENDS = ("auto", "b200", "torch")
+ATTENTION_SCHEDULES = ("auto", "two_pass", "one_pass")
 # ffn_backend="auto" fuses the FFN input projection with its GELU when the
 # projection has at least this many output elements (rows * ffn_dim); below
 # it the launch and the CTA-pair set-up outweigh the saved GELU pass.
@@ -103,12 +116,13 @@ class _RouteTally:
     exactly like eager forwards and the set-up itself counts for nothing.
     """
 
-    __slots__ = ("attention", "residual_layer_norm", "linear_gelu")
+    __slots__ = ("attention", "residual_layer_norm", "linear_gelu", "linear_residual")
 
     def __init__(self) -> None:
         self.attention: Dict[str, int] = {}
         self.residual_layer_norm = 0
         self.linear_gelu = 0
+        self.linear_residual = 0
 
     def add_attention(self, backend: str) -> None:
         self.attention[backend] = self.attention.get(backend, 0) + 1
@@ -120,6 +134,7 @@ class _RouteTally:
             )
         model.fused_residual_layer_norm_calls += self.residual_layer_norm
         model.fused_linear_gelu_calls += self.linear_gelu
+        model.fused_linear_residual_calls += self.linear_residual
 
 
 def _round_to_tf32(weight: torch.Tensor) -> torch.Tensor:
@@ -146,6 +161,8 @@ class UserOptimizedTransformer(TransformerWeights):
         execution_mode: str = "auto",
         *,
         ffn_backend: str = "auto",
+        residual_backend: str = "auto",
+        attention_schedule: str = "auto",
     ) -> None:
         super().__init__(config)
         if attention_backend not in ATTENTION_BACKENDS:
@@ -157,9 +174,20 @@ class UserOptimizedTransformer(TransformerWeights):
             raise ValueError(f"execution_mode must be one of {EXECUTION_MODES}")
         if ffn_backend not in FFN_BACKENDS:
             raise ValueError(f"ffn_backend must be one of {FFN_BACKENDS}, got {ffn_backend!r}")
+        if residual_backend not in RESIDUAL_BACKENDS:
+            raise ValueError(
+                f"residual_backend must be one of {RESIDUAL_BACKENDS}, got {residual_backend!r}"
+            )
+        if attention_schedule not in ATTENTION_SCHEDULES:
+            raise ValueError(
+                f"attention_schedule must be one of {ATTENTION_SCHEDULES}, "
+                f"got {attention_schedule!r}"
+            )
+        self.attention_schedule = attention_schedule
         self.attention_backend = attention_backend
         self.execution_mode = execution_mode
         self.ffn_backend = ffn_backend
+        self.residual_backend = residual_backend
         self._lock = threading.RLock()
         self.attention_backend_counts: Dict[str, int] = {
             CUSTOM_BACKEND: 0,
@@ -168,6 +196,7 @@ class UserOptimizedTransformer(TransformerWeights):
         }
         self.fused_residual_layer_norm_calls = 0
         self.fused_linear_gelu_calls = 0
+        self.fused_linear_residual_calls = 0
         self.cuda_graph_replays = 0
         self._captures: "OrderedDict[tuple, _CapturedForward]" = OrderedDict()
         self._host_streams: Dict[int, Tuple[torch.cuda.Stream, ...]] = {}
@@ -183,6 +212,7 @@ class UserOptimizedTransformer(TransformerWeights):
         self.attention_backend_counts = {CUSTOM_BACKEND: 0, "sdpa": 0, "reference": 0}
         self.fused_residual_layer_norm_calls = 0
         self.fused_linear_gelu_calls = 0
+        self.fused_linear_residual_calls = 0
         self.cuda_graph_replays = 0
 
     def __getstate__(self):
@@ -199,6 +229,9 @@ class UserOptimizedTransformer(TransformerWeights):
         self._lock = threading.RLock()
         self.__dict__.setdefault("ffn_backend", "auto")
         self.__dict__.setdefault("fused_linear_gelu_calls", 0)
+        self.__dict__.setdefault("residual_backend", "auto")
+        self.__dict__.setdefault("attention_schedule", "auto")
+        self.__dict__.setdefault("fused_linear_residual_calls", 0)
         self.__dict__.setdefault("_tf32_weight_cache", {})
         self.__dict__.setdefault("_captures", OrderedDict())
 
@@ -284,12 +317,15 @@ class UserOptimizedTransformer(TransformerWeights):
     def _project_qkv(
         self, attn: SelfAttentionWeights, x: torch.Tensor
     ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        """q, k, v as [B, S, H, D] views (strided views of one GEMM for fp32)."""
+        """q, k, v as [B, S, H, D] strided views of one packed GEMM
+        (F.linear with the [3d, d] concatenated weight; reference
+        submission.py:168-217). On CUDA without autograd every dtype packs:
+        each output column is the same fp32 dot product over K as in the
+        separate projection (measured bit-identical for bf16 at the BASELINE
+        shapes, tests/test_gpu_bitwise_ops.py)."""
         batch, seq_len, _ = x.shape
-        use_packed = x.is_cuda and x.dtype == torch.float32 and not torch.is_grad_enabled()
+        use_packed = x.is_cuda and not torch.is_grad_enabled()
         if not use_packed:
-            # 16-bit: the three projections are the baseline's own GEMM calls,
-            # keeping their rounding identical to the explicit model.
             return (
                 split_heads(attn.q_proj(x), attn.num_heads),
                 split_heads(attn.k_proj(x), attn.num_heads),
@@ -307,6 +343,24 @@ class UserOptimizedTransformer(TransformerWeights):
         qkv = projected.view(batch, seq_len, 3, attn.num_heads, attn.head_dim)
         return qkv.unbind(dim=2)
 
+    def _attention_context(
+        self,
+        attn: SelfAttentionWeights,
+        x: torch.Tensor,
+        valid_token_mask: Optional[torch.Tensor],
+        causal: bool,
+        tally: _RouteTally,
+    ) -> torch.Tensor:
+        """The attention output before out_proj, as [B, S, d_model]."""
+        batch, seq_len, _ = x.shape
+        q, k, v = self._project_qkv(attn, x)
+        context, dispatch = attention_forward(
+            q, k, v, valid_token_mask, causal=causal, scale=attn.scale,
+            backend=self.attention_backend, schedule=self.attention_schedule,
+        )
+        tally.add_attention(dispatch.selected)
+        return context.reshape(batch, seq_len, attn.d_model)
+
     def _attention(
         self,
         attn: SelfAttentionWeights,
@@ -315,14 +369,7 @@ class UserOptimizedTransformer(TransformerWeights):
         causal: bool,
         tally: _RouteTally,
     ) -> torch.Tensor:
-        batch, seq_len, _ = x.shape
-        q, k, v = self._project_qkv(attn, x)
-        context, dispatch = attention_forward(
-            q, k, v, valid_token_mask, causal=causal, scale=attn.scale,
-            backend=self.attention_backend,
-        )
-        tally.add_attention(dispatch.selected)
-        return attn.out_proj(context.reshape(batch, seq_len, attn.d_model))
+        return attn.out_proj(self._attention_context(attn, x, valid_token_mask, causal, tally))
 
     # ---------------------------------------------------------------- routing
     def fused_route_reason(
@@ -581,7 +628,10 @@ class UserOptimizedTransformer(TransformerWeights):
             torch.backends.cuda.matmul.allow_tf32,
             torch.is_inference_mode_enabled(),  # the boxes are inference tensors or not
         )
-        return (tuple(params), eps, self.attention_backend, self.ffn_backend, inputs)
+        return (
+            tuple(params), eps, self.attention_backend, self.ffn_backend, self.residual_backend,
+            self.attention_schedule, inputs,
+        )
 
     def _replay(self, x, valid_token_mask, key) -> torch.Tensor:
         with self._lock:
@@ -654,6 +704,46 @@ class UserOptimizedTransformer(TransformerWeights):
         tally.linear_gelu += 1
         return fused_linear_gelu(h, weight, linear.bias)
 
+    @staticmethod
+    def _gemm_reason(x: torch.Tensor, linear: nn.Linear) -> Optional[str]:
+        """Why the tcgen05 GEMM kernels cannot run ``linear`` on an input of
+        x's dtype and device (any row count), or None."""
+        reason = device_supported(x.device)
+        if reason is not None:
+            return reason
+        w, b = linear.weight, linear.bias
+        if w.dtype != x.dtype or w.device != x.device or not w.is_contiguous():
+            return "weight must be contiguous, in x's dtype, on x's device"
+        if b is not None and (b.dtype != x.dtype or not b.is_contiguous() or b.data_ptr() % 16):
+            return "bias must be contiguous, 16-byte aligned and in x's dtype"
+        elem = x.element_size()
+        if (linear.in_features * elem) % 16 or (linear.out_features * elem) % 16 or w.data_ptr() % 16:
+            return "features must be multiples of 16 bytes of elements, weight 16-byte aligned"
+        return None
+
+    def _residual_fused(self, x: torch.Tensor) -> bool:
+        """Whether out_proj and ffn_out run as GEMMs with the residual add in
+        their epilogue, for a block whose residual stream is like x. "auto"
+        fuses 16-bit models from FUSED_FFN_MIN_OUTPUTS outputs per projection
+        on; fp32 only when forced (and with TF32 matmuls allowed): an fp32
+        Linear under the harness flags multiplies TF32 operands rounded to
+        nearest, while the kernel truncates the operands it reads."""
+        if self.residual_backend == "torch":
+            return False
+        if x.dtype == torch.float32 and (
+            self.residual_backend == "auto" or not torch.backends.cuda.matmul.allow_tf32
+        ):
+            return False
+        layer = self.layers[0]
+        for linear in (layer.attention.out_proj, layer.ffn_out):
+            reason = self._gemm_reason(x, linear)
+            if reason is not None:
+                if self.residual_backend == "b200":
+                    raise ValueError(f"residual_backend='b200' cannot run this block: {reason}")
+                return False
+        outputs = x.numel()  # rows x d_model per projection
+        return self.residual_backend == "b200" or outputs >= FUSED_FFN_MIN_OUTPUTS
+
     def _fused_block(
         self,
         index: int,
@@ -665,11 +755,37 @@ class UserOptimizedTransformer(TransformerWeights):
         """Block ``index`` given its residual input x and norm1(x): returns the
         block's residual output and the next LayerNorm of it."""
         layer = self.layers[index]
-        attn_out = self._attention(
+        context = self._attention_context(
             layer.attention, normalized, valid_token_mask, self.config.causal, tally
         )
         del normalized
         fused_ffn = self._ffn_fused(layer.ffn_in, x)
+        is_last = index + 1 == len(self.layers)
+        next_norm = self.final_norm if is_last else self.layers[index + 1].norm1
+        zero_output = is_last and valid_token_mask is not None
+        if self._residual_fused(x):
+            # x + out_proj(context) and x + ffn_out(...) from the GEMM
+            # epilogues; the LayerNorms that follow read the new residual.
+            out_proj, ffn_out = layer.attention.out_proj, layer.ffn_out
+            x = fused_linear_residual(context, out_proj.weight, out_proj.bias, x)
+            del context
+            ffn_input = layer_norm(
+                x, layer.norm2.weight, layer.norm2.bias, layer.norm2.eps,
+                round_normalized_tf32=fused_ffn and x.dtype == torch.float32,
+            )
+            hidden = self._ffn_in_gelu(layer.ffn_in, ffn_input, fused_ffn, tally)
+            del ffn_input
+            # the block-end masked_fill: invalid rows of the residual are 0
+            x = fused_linear_residual(hidden, ffn_out.weight, ffn_out.bias, x, valid_token_mask)
+            del hidden
+            tally.linear_residual += 2
+            normalized = layer_norm(
+                x, next_norm.weight, next_norm.bias, next_norm.eps, valid_token_mask,
+                zero_invalid_normalized=zero_output,
+            )
+            return x, normalized
+        attn_out = layer.attention.out_proj(context)
+        del context
         x, ffn_input = self._fused_residual_norm(
             x, attn_out, layer.norm2, valid_token_mask, tally,
             round_normalized_tf32=fused_ffn and x.dtype == torch.float32,
@@ -677,14 +793,12 @@ class UserOptimizedTransformer(TransformerWeights):
         del attn_out
         ffn_out = layer.ffn_out(self._ffn_in_gelu(layer.ffn_in, ffn_input, fused_ffn, tally))
         del ffn_input
-        is_last = index + 1 == len(self.layers)
-        next_norm = self.final_norm if is_last else self.layers[index + 1].norm1
         # Invalid rows: the block-end masked_fill zeroes the residual stream,
         # and the model output is zeroed after final_norm.
         return self._fused_residual_norm(
             x, ffn_out, next_norm, valid_token_mask, tally,
             zero_invalid_residual=valid_token_mask is not None,
-            zero_invalid_normalized=is_last and valid_token_mask is not None,
+            zero_invalid_normalized=zero_output,
         )
 
     def _forward_fused(
