@@ -18,7 +18,7 @@ bool attention_tc_one_pass(int dtype, int64_t seq, float scale, int schedule) {
   // fp32 has one schedule (3xTF32, one pass). The 16-bit one-pass kernel
   // finds row maxima before scaling, which needs scale > 0.
   if (dtype == B200TK_DTYPE_FLOAT32 || !(scale > 0.f)) return false;
-  if (schedule == B200TK_SCHEDULE_ONE_PASS || schedule == 4 || schedule == 5) return true;
+  if (schedule == B200TK_SCHEDULE_ONE_PASS) return true;
   if (schedule == B200TK_SCHEDULE_TWO_PASS) return false;
   return seq >= kOnePassMinSeq;
 }
@@ -57,8 +57,6 @@ cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
   prm.scale_pow2 = a.dtype == B200TK_DTYPE_BFLOAT16 && a.scale > 0.f &&
                    std::frexp(a.scale, &exponent) == 0.5f;
   prm.one_pass = attention_tc_one_pass(a.dtype, a.seq, a.scale, a.schedule) ? 1 : 0;
-  if (prm.one_pass && (a.schedule == 4 || a.schedule == 5)) prm.one_pass = a.schedule - 1;
-  prm.exact_exp = a.schedule == 3 ? 1 : 0;
   prm.status = a.status;
   const bool causal = a.causal != 0;
   const bool has_mask = a.mask != nullptr;

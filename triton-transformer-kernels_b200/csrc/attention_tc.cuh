@@ -72,7 +72,6 @@ struct __align__(64) AttnTcParams {
   int causal_pairs;    // persistent causal schedule over (long, short) tile pairs
   int scale_pow2;      // bf16 only: scale is an exact power of two
   int one_pass;        // 16-bit only: online softmax (see TcLayout::kTwoPass)
-  int exact_exp;       // 16-bit two-pass: libm expf and IEEE division (experiment)
   unsigned int* status;
 };
 
@@ -146,36 +145,6 @@ __device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
       "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
       : "+f"(a0), "+f"(a1)
       : "f"(b0), "f"(b1));
-}
-
-// 2^x and 2^y for finite x, y <= 0 on the FMA and integer pipes instead of
-// the MUFU: Cody-Waite range reduction x = n + f with n = rint(x) (adding
-// 1.5 * 2^23 leaves n in the low mantissa bits) and f in [-1/2, 1/2], 2^f by a
-// degree-5 polynomial (coefficients fitted for this library by weighted least
-// squares on the relative error over [-1/2, 1/2]: max relative error 3.5e-7,
-// close to the hardware ex2.approx), and 2^n added to the exponent field.
-// Arguments are clamped at -126 (a result below 2^-126 is flushed to zero
-// by the hardware path; here it is at most 2^-126, far below the rounding of
-// any probability that is added to a row sum of at least 1).
-__device__ __forceinline__ void exp2_fma2(float& x, float& y) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  x = fmaxf(x, -126.0f);
-  y = fmaxf(y, -126.0f);
-  float tx = x, ty = y;
-  add2(tx, ty, kShift, kShift);         // rint(x) + shift
-  float nx = tx, ny = ty;
-  add2(nx, ny, -kShift, -kShift);       // rint(x)
-  float fx = x, fy = y;
-  add2(fx, fy, -nx, -ny);               // f = x - rint(x)
-  float px = 1.2915670e-3f, py = 1.2915670e-3f;
-  fma2(px, py, fx, fy, 9.6685309e-3f, 9.6685309e-3f);
-  fma2(px, py, fx, fy, 5.5516887e-2f, 5.5516887e-2f);
-  fma2(px, py, fx, fy, 2.4022265e-1f, 2.4022265e-1f);
-  fma2(px, py, fx, fy, 6.9314647e-1f, 6.9314647e-1f);
-  fma2(px, py, fx, fy, 1.0f, 1.0f);
-  // the integer part sits in the low bits of t: add it to the exponent
-  x = __uint_as_float(__float_as_uint(px) + ((__float_as_uint(tx) - 0x4B400000u) << 23));
-  y = __uint_as_float(__float_as_uint(py) + ((__float_as_uint(ty) - 0x4B400000u) << 23));
 }
 
 // Round two fp32 values to T and pack them (a in the low half).
@@ -313,18 +282,11 @@ struct TcLayout {
   static_assert(!kSplit || NQ == 1, "fp32 keeps one query tile per CTA");
 };
 
-// SCHED: 0 two-pass, 1 one-pass (16-bit), 2 two-pass with libm expf and IEEE
-// division (16-bit, experimental).
-template <typename T, int D, int BN, int KST, int VST, int NQ, int SCHED, bool CAUSAL,
+template <typename T, int D, int BN, int KST, int VST, int NQ, bool OP, bool CAUSAL,
           bool HAS_MASK>
-__global__ void __launch_bounds__(
-    TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1 || SCHED >= 3>::kThreads, 1)
+__global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads, 1)
     attention_fwd_tc_kernel(const __grid_constant__ AttnTcParams p) {
-  using L = TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1 || SCHED >= 3>;
-  constexpr bool kExactExp = SCHED == 2;
-  // one-pass: every kPolyEvery-th probability pair of an unmasked tile is
-  // exponentiated on the FMA pipe (exp2_fma2) instead of the MUFU (0: none)
-  constexpr int kPolyEvery = SCHED == 3 ? 4 : SCHED == 4 ? 2 : 0;
+  using L = TcLayout<T, D, BN, KST, VST, NQ, OP>;
   constexpr bool kSplit = L::kSplit;
   constexpr int NSB = L::kNSB;
   constexpr bool kTwoPass = L::kTwoPass;
@@ -874,7 +836,6 @@ __global__ void __launch_bounds__(
         float m_run = -INFINITY;  // running max of this half, log2 units
         float l_run = 0.f;
         float m_fin = 0.f, inv_l = 0.f;  // row max (log2 units) and 1/row sum
-        float l_fin = 0.f;               // row sum
 
         for (int g = 0; g < w.n_s && ok; ++g) {
           const int sg = kc + g;
@@ -973,28 +934,17 @@ __global__ void __launch_bounds__(
 
           if (!pass2) {
             // pass 1: running max and sum of this half
-            constexpr bool ex = kExactExp;
-            const float m_new = fmaxf(m_run, ex ? mx : mx * kLog2e);
+            const float m_new = fmaxf(m_run, mx * kLog2e);
             const float m_use = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = m_run == -INFINITY ? 0.f
-                                : ex               ? expf(m_run - m_use)
-                                                   : ex2_approx(m_run - m_use);
+            const float alpha = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_use);
             float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if constexpr (ex) {
 #pragma unroll
-              for (int i = 0; i < HB; i += 2) {
-                const float a = expf(sv[i] - m_use), c = expf(sv[i + 1] - m_use);
-                add2(part[i % 8], part[i % 8 + 1], a, c);
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < HB; i += 2) {
-                float a = sv[i], c = sv[i + 1];
-                fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
-                a = ex2_approx(a);
-                c = ex2_approx(c);
-                add2(part[i % 8], part[i % 8 + 1], a, c);
-              }
+            for (int i = 0; i < HB; i += 2) {
+              float a = sv[i], c = sv[i + 1];
+              fma2(a, c, kLog2e, kLog2e, -m_use, -m_use);
+              a = ex2_approx(a);
+              c = ex2_approx(c);
+              add2(part[i % 8], part[i % 8 + 1], a, c);
             }
             add2(part[0], part[1], part[2], part[3]);
             add2(part[4], part[5], part[6], part[7]);
@@ -1011,40 +961,26 @@ __global__ void __launch_bounds__(
               const float2 other = stats[(t * 2 + (half ^ 1)) * BM + r];
               const float mm = fmaxf(m_run, other.x);
               const float mu = mm == -INFINITY ? 0.f : mm;
-              const float la = m_run == -INFINITY ? 0.f
-                               : ex               ? l_run * expf(m_run - mu)
-                                                  : l_run * ex2_approx(m_run - mu);
-              const float lb = other.x == -INFINITY ? 0.f
-                               : ex                 ? other.y * expf(other.x - mu)
-                                                    : other.y * ex2_approx(other.x - mu);
+              const float la = m_run == -INFINITY ? 0.f : l_run * ex2_approx(m_run - mu);
+              const float lb = other.x == -INFINITY ? 0.f : other.y * ex2_approx(other.x - mu);
               // same association on both threads of the row: (half 0) + (half 1)
               const float l = half == 0 ? la + lb : lb + la;
               m_fin = mu;
               inv_l = l > 0.f ? 1.f / l : 0.f;
-              l_fin = l;
             }
             continue;
           }
 
           // pass 2: normalised probabilities, rounded to T, into TMEM
           uint32_t pk[HB / 2];
-          if constexpr (kExactExp) {
 #pragma unroll
-            for (int i = 0; i < HB; i += 2) {
-              const float a = l_fin > 0.f ? __fdiv_rn(expf(sv[i] - m_fin), l_fin) : 0.f;
-              const float c = l_fin > 0.f ? __fdiv_rn(expf(sv[i + 1] - m_fin), l_fin) : 0.f;
-              pk[i / 2] = cvt_pack2<T>(a, c);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < HB; i += 2) {
-              float a = sv[i], c = sv[i + 1];
-              fma2(a, c, kLog2e, kLog2e, -m_fin, -m_fin);
-              a = ex2_approx(a);
-              c = ex2_approx(c);
-              mul2(a, c, inv_l, inv_l);
-              pk[i / 2] = cvt_pack2<T>(a, c);
-            }
+          for (int i = 0; i < HB; i += 2) {
+            float a = sv[i], c = sv[i + 1];
+            fma2(a, c, kLog2e, kLog2e, -m_fin, -m_fin);
+            a = ex2_approx(a);
+            c = ex2_approx(c);
+            mul2(a, c, inv_l, inv_l);
+            pk[i / 2] = cvt_pack2<T>(a, c);
           }
           if (j > 0) {
             // Waiting for every P@V phase in order keeps the pv_done parity
@@ -1163,7 +1099,6 @@ __global__ void __launch_bounds__(
           tc_fence_after();
           const int n0 = j * BN;
           uint32_t pk[NP];  // T(qk) pairs; pair i belongs to row ra + 8 * (i & 1)
-          bool tile_masked;
           {
             uint32_t raw[NE];
             tmem_ld16x256b<8>(tmem + lane_off + L::t_s(t, buf), raw);
@@ -1184,8 +1119,9 @@ __global__ void __launch_bounds__(
 #pragma unroll
               for (int wd = 0; wd < BN / 32; ++wd) pad = pad || kbits[wd] != 0xFFFFFFFFu;
             }
-            tile_masked = pad || (n0 + BN > p.seq) || (CAUSAL && n0 + BN - 1 > row0 + rb);
-            if (tile_masked) {
+            const bool masked =
+                pad || (n0 + BN > p.seq) || (CAUSAL && n0 + BN - 1 > row0 + rb);
+            if (masked) {
 #pragma unroll
               for (int e = 0; e < NE; ++e) {
                 const int c = e_col(e);
@@ -1272,12 +1208,8 @@ __global__ void __launch_bounds__(
               round_pair<T>(a, c);
               fma2(a, c, kLog2e, kLog2e, -m_use[h], -m_use[h]);
             }
-            if (kPolyEvery > 0 && i % kPolyEvery == kPolyEvery - 1 && !tile_masked) {
-              exp2_fma2(a, c);
-            } else {
-              a = ex2_approx(a);
-              c = ex2_approx(c);
-            }
+            a = ex2_approx(a);
+            c = ex2_approx(c);
             add2(part[h][0], part[h][1], a, c);
             pk[i] = cvt_pack2<T>(a, c);
           }
@@ -1556,11 +1488,11 @@ __global__ void __launch_bounds__(
   }
 }
 
-template <typename T, int D, int BN, int KST, int VST, int NQ, int SCHED, bool CAUSAL,
+template <typename T, int D, int BN, int KST, int VST, int NQ, bool OP, bool CAUSAL,
           bool HAS_MASK>
 cudaError_t launch_tc(const AttnTcParams& prm, int grid, cudaStream_t stream) {
-  using L = TcLayout<T, D, BN, KST, VST, NQ, SCHED == 1 || SCHED >= 3>;
-  auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, SCHED, CAUSAL, HAS_MASK>;
+  using L = TcLayout<T, D, BN, KST, VST, NQ, OP>;
+  auto kernel = attention_fwd_tc_kernel<T, D, BN, KST, VST, NQ, OP, CAUSAL, HAS_MASK>;
   // at least ~116 KB so that one CTA (and one TMEM allocation) owns each SM
   const int smem = L::kBytes > 118 * 1024 ? L::kBytes : 118 * 1024;
   // The opt-in shared-memory size is set once per device and instantiation,
@@ -1597,7 +1529,7 @@ struct TcTile<float, 128> {
   static constexpr int kNQ = 1, kBN = 32, kKST = 2, kVST = 2;
 };
 
-template <typename T, int D, int OP>
+template <typename T, int D, bool OP>
 cudaError_t launch_variant(const AttnTcParams& prm, int grid, bool causal, bool has_mask,
                            cudaStream_t stream) {
   using C = TcTile<T, D>;
@@ -1638,12 +1570,9 @@ cudaError_t launch_dtype_hd(AttnTcParams prm, int num_sms, bool causal, bool has
   const bool persistent = !causal || prm.causal_pairs;
   const int grid = static_cast<int>(persistent ? (work < num_sms ? work : num_sms) : work);
   if constexpr (!std::is_same_v<T, float>) {
-    if (prm.one_pass == 3) return launch_variant<T, D, 3>(prm, grid, causal, has_mask, stream);
-    if (prm.one_pass == 4) return launch_variant<T, D, 4>(prm, grid, causal, has_mask, stream);
-    if (prm.one_pass) return launch_variant<T, D, 1>(prm, grid, causal, has_mask, stream);
-    if (prm.exact_exp) return launch_variant<T, D, 2>(prm, grid, causal, has_mask, stream);
+    if (prm.one_pass) return launch_variant<T, D, true>(prm, grid, causal, has_mask, stream);
   }
-  return launch_variant<T, D, 0>(prm, grid, causal, has_mask, stream);
+  return launch_variant<T, D, false>(prm, grid, causal, has_mask, stream);
 }
 
 // Explicit instantiations live in attention_tc_inst.cu, compiled once per

@@ -263,7 +263,7 @@ int b200tk_attention_fwd_scheduled(const void* q, const int64_t* q_strides, cons
                                    int64_t head_dim, int causal, float scale, int schedule,
                                    void* stream) {
   if (schedule != B200TK_SCHEDULE_AUTO && schedule != B200TK_SCHEDULE_TWO_PASS &&
-      schedule != B200TK_SCHEDULE_ONE_PASS && (schedule < 3 || schedule > 5))
+      schedule != B200TK_SCHEDULE_ONE_PASS)
     return fail(B200TK_ERR_INVALID_ARGUMENT, "unknown attention schedule");
   int rc = validate_attention(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len,
                               heads, head_dim);

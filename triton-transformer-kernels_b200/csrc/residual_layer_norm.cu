@@ -361,16 +361,25 @@ struct Quad {  // 4 consecutive elements: 16 bytes (fp32) or 8 bytes (16-bit)
   }
 };
 
-constexpr int kWelfordThreads = 128;  // threads per row (4 warps)
+// ATen's kernel uses 128 threads per row; here one warp computes a row, lane
+// l standing in for those threads l, l + 32, l + 64 and l + 96 ("virtual
+// threads", one per ATen warp w = 0..3): each keeps its own Welford state over
+// exactly the elements that ATen thread would fold, the shuffle-down
+// combination runs once per virtual warp (lanes hold the same virtual-thread
+// index), and lane 0 then folds virtual warps 2, 3 into 0, 1 and 1 into 0 --
+// the inter-warp tree of ATen's kernel, in registers. 8 rows per 256-thread
+// CTA; no shared memory and no block barrier. The output pass re-reads the
+// row (L2-resident) instead of holding it in registers.
+constexpr int kAtenThreads = 128;  // ATen's threads per row (4 warps)
+constexpr int kWelfordRowsPerCta = 8;
 
-template <typename T, int NQ>  // NQ: 4-element groups per thread (width <= 512 * NQ)
-__global__ void __launch_bounds__(kWelfordThreads) rln_welford_kernel(const RlnArgs a) {
+template <typename T, int QPV>  // QPV: 4-element groups per ATen thread (width <= 512 * QPV)
+__global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(const RlnArgs a) {
   using Q = Quad<T>;
   using Raw = typename Q::Raw;
-  __shared__ float xch[8];
-  const int t = threadIdx.x;
-  const int lane = t & 31, warp = t >> 5;
-  const int64_t row = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWelfordRowsPerCta + (threadIdx.x >> 5);
+  if (row >= a.rows) return;  // whole warps leave together
   const int n_quads = static_cast<int>(a.width / 4);
   const bool has_update = !(a.flags & B200TK_RLN_NO_UPDATE);
   bool valid = true;
@@ -382,96 +391,104 @@ __global__ void __launch_bounds__(kWelfordThreads) rln_welford_kernel(const RlnA
   const Raw* uq = reinterpret_cast<const Raw*>(static_cast<const T*>(a.update) + row * a.width);
   Raw* rq = reinterpret_cast<Raw*>(static_cast<T*>(a.residual_out) + row * a.width);
   Raw* nq = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + row * a.width);
-
-  Raw xr[NQ], ur[NQ];
-#pragma unroll
-  for (int i = 0; i < NQ; ++i) {
-    const int qi = i * kWelfordThreads + t;
-    const bool in = qi < n_quads;
-    xr[i] = in ? xq[qi] : Raw{};
-    ur[i] = (in && has_update) ? uq[qi] : Raw{};
-  }
-  float r[NQ][4];
-  WelfordState st{0.f, 0.f, 0.f};
-#pragma unroll
-  for (int i = 0; i < NQ; ++i) {
-    const int qi = i * kWelfordThreads + t;
-    if (qi >= n_quads) break;  // later groups of this thread are past the row too
+  // the residual element value, rounded to T (zero on a zeroed row)
+  auto residual = [&](const Raw& xv, const Raw& uv, float (&r)[4]) {
     float fx[4], fu[4];
-    Q::unpack(xr[i], fx);
-    Q::unpack(ur[i], fu);
+    Q::unpack(xv, fx);
+    Q::unpack(uv, fu);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       float v = has_update ? fx[e] + fu[e] : fx[e];
       if constexpr (!std::is_same_v<T, float>) v = round_t<T>(v);
-      r[i][e] = zero_res ? 0.f : v;
-      // the count before this element is 4 * i + e: 1 / (4 * i + e + 1) folds
-      // to a correctly rounded constant
-      st = welford_add(st, r[i][e], 1.f / static_cast<float>(4 * i + e + 1));
+      r[e] = zero_res ? 0.f : v;
     }
-    if (has_update) rq[qi] = Q::pack(r[i]);
+  };
+
+  WelfordState st[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) st[w] = WelfordState{0.f, 0.f, 0.f};
+#pragma unroll
+  for (int k = 0; k < QPV; ++k) {
+    // this step's group of every virtual thread, loaded before any is folded
+    Raw xv[4], uv[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int qi = lane + 32 * w + kAtenThreads * k;
+      const bool in = qi < n_quads;
+      xv[w] = in ? xq[qi] : Raw{};
+      uv[w] = (in && has_update) ? uq[qi] : Raw{};
+    }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int qi = lane + 32 * w + kAtenThreads * k;
+      if (qi >= n_quads) continue;
+      float r[4];
+      residual(xv[w], uv[w], r);
+      // the count before element e of group k is 4k + e: 1 / (4k + e + 1)
+      // folds to a correctly rounded constant
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        st[w] = welford_add(st[w], r[e], 1.f / static_cast<float>(4 * k + e + 1));
+      if (has_update) rq[qi] = Q::pack(r);
+    }
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
-    const WelfordState o{__shfl_down_sync(0xFFFFFFFFu, st.mean, off),
-                         __shfl_down_sync(0xFFFFFFFFu, st.m2, off),
-                         __shfl_down_sync(0xFFFFFFFFu, st.count, off)};
-    st = welford_combine(st, o);
-  }
-  // warps 2, 3 -> 0, 1; then 1 -> 0 (lane 0 of each warp holds its state)
 #pragma unroll
-  for (int off = 2; off > 0; off >>= 1) {
-    if (lane == 0 && warp >= off && warp < 2 * off) {
-      xch[3 * (warp - off)] = st.mean;
-      xch[3 * (warp - off) + 1] = st.m2;
-      xch[3 * (warp - off) + 2] = st.count;
+    for (int w = 0; w < 4; ++w) {
+      const WelfordState o{__shfl_down_sync(0xFFFFFFFFu, st[w].mean, off),
+                           __shfl_down_sync(0xFFFFFFFFu, st[w].m2, off),
+                           __shfl_down_sync(0xFFFFFFFFu, st[w].count, off)};
+      st[w] = welford_combine(st[w], o);
     }
-    __syncthreads();
-    if (lane == 0 && warp < off)
-      st = welford_combine(st, WelfordState{xch[3 * warp], xch[3 * warp + 1], xch[3 * warp + 2]});
-    __syncthreads();
   }
-  if (t == 0) {
-    xch[6] = st.mean;
-    xch[7] = __fdiv_rn(st.m2, static_cast<float>(a.width));
-  }
-  __syncthreads();
-  const float mean = xch[6];
-  const float rstd = rsqrtf(__fadd_rn(xch[7], a.eps));
+  // lane 0: ATen's inter-warp tree (2, 3 -> 0, 1; then 1 -> 0)
+  st[0] = welford_combine(st[0], st[2]);
+  st[1] = welford_combine(st[1], st[3]);
+  st[0] = welford_combine(st[0], st[1]);
+  const float mean = __shfl_sync(0xFFFFFFFFu, st[0].mean, 0);
+  const float var = __fdiv_rn(__shfl_sync(0xFFFFFFFFu, st[0].m2, 0), static_cast<float>(a.width));
+  const float rstd = rsqrtf(__fadd_rn(var, a.eps));
   const Raw* wq = static_cast<const Raw*>(a.weight);
   const Raw* bq = static_cast<const Raw*>(a.bias);
 #pragma unroll
-  for (int i = 0; i < NQ; ++i) {
-    const int qi = i * kWelfordThreads + t;
-    if (qi >= n_quads) break;
-    float fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f}, o[4];
-    Q::unpack(wq[qi], fw);
-    if (bq != nullptr) Q::unpack(bq[qi], fb);
+  for (int k = 0; k < QPV; ++k) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float c = __fmul_rn(rstd, __fsub_rn(r[i][e], mean));
-      const float nrm = bq != nullptr ? __fmaf_rn(fw[e], c, fb[e]) : __fmul_rn(fw[e], c);
-      o[e] = zero_norm ? 0.f : (tf32 ? round_tf32(nrm) : nrm);
+    for (int w = 0; w < 4; ++w) {
+      const int qi = lane + 32 * w + kAtenThreads * k;
+      if (qi >= n_quads) continue;
+      float r[4], fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f}, o[4];
+      residual(xq[qi], has_update ? uq[qi] : Raw{}, r);
+      Q::unpack(wq[qi], fw);
+      if (bq != nullptr) Q::unpack(bq[qi], fb);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float c = __fmul_rn(rstd, __fsub_rn(r[e], mean));
+        const float nrm = bq != nullptr ? __fmaf_rn(fw[e], c, fb[e]) : __fmul_rn(fw[e], c);
+        o[e] = zero_norm ? 0.f : (tf32 ? round_tf32(nrm) : nrm);
+      }
+      nq[qi] = Q::pack(o);
     }
-    nq[qi] = Q::pack(o);
   }
 }
 
 template <typename T>
 cudaError_t launch_welford(const RlnArgs& a, cudaStream_t stream) {
   const int64_t quads = a.width / 4;
-  const int nq = static_cast<int>((quads + kWelfordThreads - 1) / kWelfordThreads);
-  if (a.rows > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
-  const unsigned grid = static_cast<unsigned>(a.rows);
-  switch (nq) {
-    case 1: rln_welford_kernel<T, 1><<<grid, kWelfordThreads, 0, stream>>>(a); break;
-    case 2: rln_welford_kernel<T, 2><<<grid, kWelfordThreads, 0, stream>>>(a); break;
-    case 3: rln_welford_kernel<T, 3><<<grid, kWelfordThreads, 0, stream>>>(a); break;
-    case 4: rln_welford_kernel<T, 4><<<grid, kWelfordThreads, 0, stream>>>(a); break;
-    case 5: rln_welford_kernel<T, 5><<<grid, kWelfordThreads, 0, stream>>>(a); break;
-    case 6: rln_welford_kernel<T, 6><<<grid, kWelfordThreads, 0, stream>>>(a); break;
-    case 7: rln_welford_kernel<T, 7><<<grid, kWelfordThreads, 0, stream>>>(a); break;
-    case 8: rln_welford_kernel<T, 8><<<grid, kWelfordThreads, 0, stream>>>(a); break;
+  const int qpv = static_cast<int>((quads + kAtenThreads - 1) / kAtenThreads);
+  const int64_t grid = (a.rows + kWelfordRowsPerCta - 1) / kWelfordRowsPerCta;
+  if (grid > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
+  const unsigned g = static_cast<unsigned>(grid);
+  constexpr int kBlock = 32 * kWelfordRowsPerCta;
+  switch (qpv) {
+    case 1: rln_welford_kernel<T, 1><<<g, kBlock, 0, stream>>>(a); break;
+    case 2: rln_welford_kernel<T, 2><<<g, kBlock, 0, stream>>>(a); break;
+    case 3: rln_welford_kernel<T, 3><<<g, kBlock, 0, stream>>>(a); break;
+    case 4: rln_welford_kernel<T, 4><<<g, kBlock, 0, stream>>>(a); break;
+    case 5: rln_welford_kernel<T, 5><<<g, kBlock, 0, stream>>>(a); break;
+    case 6: rln_welford_kernel<T, 6><<<g, kBlock, 0, stream>>>(a); break;
+    case 7: rln_welford_kernel<T, 7><<<g, kBlock, 0, stream>>>(a); break;
+    case 8: rln_welford_kernel<T, 8><<<g, kBlock, 0, stream>>>(a); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -555,7 +572,7 @@ cudaError_t launch_typed(const RlnArgs& a, cudaStream_t stream) {
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   // Rows of whole 4-element groups, up to 4096 wide, take the Welford path
   // (statistics in ATen's order); wider or unaligned rows the paths below.
-  const bool welford_ok = a.width % 4 == 0 && a.width <= 4 * kWelfordThreads * 8 &&
+  const bool welford_ok = a.width % 4 == 0 && a.width <= 4 * kAtenThreads * 8 &&
                           aligned(a.x) && aligned(a.weight) && aligned(a.normalized_out) &&
                           (a.bias == nullptr || aligned(a.bias)) &&
                           ((a.flags & B200TK_RLN_NO_UPDATE) ||

@@ -33,7 +33,7 @@ RLN_ROUND_TF32 = 8
 STATUS_PIPELINE_TIMEOUT = 1
 STATUS_SELFTEST_TIMEOUT = 2
 
-SCHEDULES = {"auto": 0, "two_pass": 1, "one_pass": 2, "exact_exp": 3}
+SCHEDULES = {"auto": 0, "two_pass": 1, "one_pass": 2}
 
 ROUTE_TCGEN05 = 1
 ROUTE_GENERIC = 2
