@@ -363,20 +363,63 @@ struct Quad {  // 4 consecutive elements: 16 bytes (fp32) or 8 bytes (16-bit)
 
 // ATen's kernel uses 128 threads per row; here one warp computes a row, lane
 // l standing in for those threads l, l + 32, l + 64 and l + 96 ("virtual
-// threads", one per ATen warp w = 0..3): each keeps its own Welford state over
-// exactly the elements that ATen thread would fold, the shuffle-down
-// combination runs once per virtual warp (lanes hold the same virtual-thread
-// index), and lane 0 then folds virtual warps 2, 3 into 0, 1 and 1 into 0 --
-// the inter-warp tree of ATen's kernel, in registers. 8 rows per 256-thread
-// CTA; no shared memory and no block barrier. The output pass re-reads the
-// row (L2-resident) instead of holding it in registers.
+// threads" 32w + l, w = 0..3 being ATen's warp): each keeps its own Welford
+// state over exactly the elements that ATen thread folds. The combination is
+// the same binary tree as ATen's -- per ATen warp w the shuffle-down levels
+// N16[w][l] = C(leaf[w][l], leaf[w][l + 16]), N8 = C(N16[l], N16[l + 8]), ...,
+// N1[w]; then C(N1[0], N1[2]), C(N1[1], N1[3]) and their combination, C(own,
+// other) with "own" the lower index -- with its nodes spread over the lanes
+// (2 + 1 + 1 + 1 + 1 + 2 combinations per lane instead of 4 per shuffle level)
+// because a combination costs a correctly rounded reciprocal. 8 rows per
+// 256-thread CTA; no shared memory and no block barrier. Rows of at most 1024
+// elements stay in registers between the passes; longer ones are re-read
+// (L2-resident).
 constexpr int kAtenThreads = 128;  // ATen's threads per row (4 warps)
 constexpr int kWelfordRowsPerCta = 8;
+
+__device__ __forceinline__ WelfordState shfl_state(const WelfordState& v, int src) {
+  return {__shfl_sync(0xFFFFFFFFu, v.mean, src), __shfl_sync(0xFFFFFFFFu, v.m2, src),
+          __shfl_sync(0xFFFFFFFFu, v.count, src)};
+}
+__device__ __forceinline__ WelfordState shfl_xor_state(const WelfordState& v, int mask) {
+  return {__shfl_xor_sync(0xFFFFFFFFu, v.mean, mask), __shfl_xor_sync(0xFFFFFFFFu, v.m2, mask),
+          __shfl_xor_sync(0xFFFFFFFFu, v.count, mask)};
+}
+__device__ __forceinline__ WelfordState shfl_down_state(const WelfordState& v, int off) {
+  return {__shfl_down_sync(0xFFFFFFFFu, v.mean, off), __shfl_down_sync(0xFFFFFFFFu, v.m2, off),
+          __shfl_down_sync(0xFFFFFFFFu, v.count, off)};
+}
+
+// The root of ATen's combination tree over the 128 virtual-thread states
+// leaf[w] (this lane's virtual threads 32w + lane); valid in lane 0.
+__device__ __forceinline__ WelfordState welford_tree(const WelfordState (&leaf)[4], int lane) {
+  // N16: lane j < 16 builds (w = 0, 2; l = j), lane j >= 16 (w = 1, 3; l = j - 16).
+  // The partner lane j ^ 16 holds the other leaf of each pair.
+  const bool lo = lane < 16;
+  const WelfordState ra = shfl_xor_state(lo ? leaf[1] : leaf[0], 16);
+  const WelfordState rb = shfl_xor_state(lo ? leaf[3] : leaf[2], 16);
+  const WelfordState x = lo ? welford_combine(leaf[0], ra) : welford_combine(ra, leaf[1]);
+  const WelfordState y = lo ? welford_combine(leaf[2], rb) : welford_combine(rb, leaf[3]);
+  // N8[w][l] (l < 8) in lane 8w + l: N16[w][l] and N16[w][l + 8] sit in lanes
+  // l + 16 (w & 1) and l + 8 + 16 (w & 1), in x for w < 2 and y for w >= 2.
+  const int w = lane >> 3, l = lane & 7;
+  const int s1 = l + 16 * (w & 1), s2 = s1 + 8;
+  const WelfordState x1 = shfl_state(x, s1), x2 = shfl_state(x, s2);
+  const WelfordState y1 = shfl_state(y, s1), y2 = shfl_state(y, s2);
+  WelfordState n = w < 2 ? welford_combine(x1, x2) : welford_combine(y1, y2);
+  // N4, N2, N1 within each group of 8 lanes (lane 8w holds N1[w])
+#pragma unroll
+  for (int off = 4; off > 0; off >>= 1) n = welford_combine(n, shfl_down_state(n, off));
+  // C(N1[0], N1[2]) in lane 0, C(N1[1], N1[3]) in lane 8, then C(that, that)
+  n = welford_combine(n, shfl_down_state(n, 16));
+  return welford_combine(n, shfl_down_state(n, 8));
+}
 
 template <typename T, int QPV>  // QPV: 4-element groups per ATen thread (width <= 512 * QPV)
 __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(const RlnArgs a) {
   using Q = Quad<T>;
   using Raw = typename Q::Raw;
+  constexpr bool kHold = QPV <= 2;  // keep the row in registers between the passes
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWelfordRowsPerCta + (threadIdx.x >> 5);
   if (row >= a.rows) return;  // whole warps leave together
@@ -391,19 +434,8 @@ __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(co
   const Raw* uq = reinterpret_cast<const Raw*>(static_cast<const T*>(a.update) + row * a.width);
   Raw* rq = reinterpret_cast<Raw*>(static_cast<T*>(a.residual_out) + row * a.width);
   Raw* nq = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + row * a.width);
-  // the residual element value, rounded to T (zero on a zeroed row)
-  auto residual = [&](const Raw& xv, const Raw& uv, float (&r)[4]) {
-    float fx[4], fu[4];
-    Q::unpack(xv, fx);
-    Q::unpack(uv, fu);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float v = has_update ? fx[e] + fu[e] : fx[e];
-      if constexpr (!std::is_same_v<T, float>) v = round_t<T>(v);
-      r[e] = zero_res ? 0.f : v;
-    }
-  };
 
+  float held[kHold ? QPV * 4 * 4 : 1];
   WelfordState st[4];
 #pragma unroll
   for (int w = 0; w < 4; ++w) st[w] = WelfordState{0.f, 0.f, 0.f};
@@ -423,34 +455,39 @@ __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(co
       const int qi = lane + 32 * w + kAtenThreads * k;
       if (qi >= n_quads) continue;
       float r[4];
-      residual(xv[w], uv[w], r);
+      Q::unpack(xv[w], r);
+      if (has_update) {
+        float fu[4];
+        Q::unpack(uv[w], fu);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float v = r[e] + fu[e];
+          if constexpr (!std::is_same_v<T, float>) v = round_t<T>(v);
+          r[e] = v;
+        }
+      }
+      if (zero_res) r[0] = r[1] = r[2] = r[3] = 0.f;
       // the count before element e of group k is 4k + e: 1 / (4k + e + 1)
       // folds to a correctly rounded constant
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         st[w] = welford_add(st[w], r[e], 1.f / static_cast<float>(4 * k + e + 1));
       if (has_update) rq[qi] = Q::pack(r);
+      if constexpr (kHold) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) held[(k * 4 + w) * 4 + e] = r[e];
+      }
     }
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const WelfordState o{__shfl_down_sync(0xFFFFFFFFu, st[w].mean, off),
-                           __shfl_down_sync(0xFFFFFFFFu, st[w].m2, off),
-                           __shfl_down_sync(0xFFFFFFFFu, st[w].count, off)};
-      st[w] = welford_combine(st[w], o);
-    }
-  }
-  // lane 0: ATen's inter-warp tree (2, 3 -> 0, 1; then 1 -> 0)
-  st[0] = welford_combine(st[0], st[2]);
-  st[1] = welford_combine(st[1], st[3]);
-  st[0] = welford_combine(st[0], st[1]);
-  const float mean = __shfl_sync(0xFFFFFFFFu, st[0].mean, 0);
-  const float var = __fdiv_rn(__shfl_sync(0xFFFFFFFFu, st[0].m2, 0), static_cast<float>(a.width));
+  const WelfordState root = welford_tree(st, lane);
+  const float mean = __shfl_sync(0xFFFFFFFFu, root.mean, 0);
+  const float var = __fdiv_rn(__shfl_sync(0xFFFFFFFFu, root.m2, 0), static_cast<float>(a.width));
   const float rstd = rsqrtf(__fadd_rn(var, a.eps));
   const Raw* wq = static_cast<const Raw*>(a.weight);
   const Raw* bq = static_cast<const Raw*>(a.bias);
+  // the second pass reads the rounded residual back (residual_out, or x
+  // itself for a plain LayerNorm) unless the row is held in registers
+  const Raw* src = has_update ? static_cast<const Raw*>(rq) : xq;
 #pragma unroll
   for (int k = 0; k < QPV; ++k) {
 #pragma unroll
@@ -458,7 +495,13 @@ __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(co
       const int qi = lane + 32 * w + kAtenThreads * k;
       if (qi >= n_quads) continue;
       float r[4], fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f}, o[4];
-      residual(xq[qi], has_update ? uq[qi] : Raw{}, r);
+      if constexpr (kHold) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) r[e] = held[(k * 4 + w) * 4 + e];
+      } else {
+        Q::unpack(src[qi], r);
+        if (zero_res) r[0] = r[1] = r[2] = r[3] = 0.f;
+      }
       Q::unpack(wq[qi], fw);
       if (bq != nullptr) Q::unpack(bq[qi], fb);
 #pragma unroll
