@@ -415,6 +415,34 @@ __device__ __forceinline__ WelfordState welford_tree(const WelfordState (&leaf)[
   return welford_combine(n, shfl_down_state(n, 8));
 }
 
+// Two fp32 values per instruction (sm_100 f32x2): each lane of the pair is
+// rounded exactly as the scalar operation, so paired arithmetic is bit-for-bit
+// the scalar arithmetic on each half.
+__device__ __forceinline__ float2 add_x2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul_x2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "mul.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma_x2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "mov.b64 z, {%6, %7};\n\tfma.rn.f32x2 x, x, y, z;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 template <typename T, int QPV>  // QPV: 4-element groups per ATen thread (width <= 512 * QPV)
 __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(const RlnArgs a) {
   using Q = Quad<T>;
@@ -436,9 +464,9 @@ __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(co
   Raw* nq = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + row * a.width);
 
   float held[kHold ? QPV * 4 * 4 : 1];
-  WelfordState st[4];
-#pragma unroll
-  for (int w = 0; w < 4; ++w) st[w] = WelfordState{0.f, 0.f, 0.f};
+  // Welford states of the virtual threads w = 0..3 as two pairs (w = 2p, 2p + 1)
+  // updated together with f32x2 arithmetic; the element counts are known.
+  float2 mean2[2] = {{0.f, 0.f}, {0.f, 0.f}}, m2_2[2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
   for (int k = 0; k < QPV; ++k) {
     // this step's group of every virtual thread, loaded before any is folded
@@ -450,34 +478,63 @@ __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(co
       xv[w] = in ? xq[qi] : Raw{};
       uv[w] = (in && has_update) ? uq[qi] : Raw{};
     }
+    float r[4][4];
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const int qi = lane + 32 * w + kAtenThreads * k;
-      if (qi >= n_quads) continue;
-      float r[4];
-      Q::unpack(xv[w], r);
+      Q::unpack(xv[w], r[w]);
       if (has_update) {
         float fu[4];
         Q::unpack(uv[w], fu);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float v = r[e] + fu[e];
+          float v = r[w][e] + fu[e];
           if constexpr (!std::is_same_v<T, float>) v = round_t<T>(v);
-          r[e] = v;
+          r[w][e] = v;
         }
       }
-      if (zero_res) r[0] = r[1] = r[2] = r[3] = 0.f;
-      // the count before element e of group k is 4k + e: 1 / (4k + e + 1)
-      // folds to a correctly rounded constant
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        st[w] = welford_add(st[w], r[e], 1.f / static_cast<float>(4 * k + e + 1));
-      if (has_update) rq[qi] = Q::pack(r);
+      if (zero_res) r[w][0] = r[w][1] = r[w][2] = r[w][3] = 0.f;
+      const int qi = lane + 32 * w + kAtenThreads * k;
+      if (has_update && qi < n_quads) rq[qi] = Q::pack(r[w]);
       if constexpr (kHold) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) held[(k * 4 + w) * 4 + e] = r[e];
+        for (int e = 0; e < 4; ++e) held[(k * 4 + w) * 4 + e] = r[w][e];
       }
     }
+    // fold: the count before element e of group k is 4k + e, so 1 / (4k + e
+    // + 1) folds to a correctly rounded constant
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+      const int q0 = lane + 32 * (2 * pr) + kAtenThreads * k;  // the pair's first group
+      if (q0 >= n_quads) continue;
+      if (q0 + 32 < n_quads) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float inv = 1.f / static_cast<float>(4 * k + e + 1);
+          const float2 v = make_float2(r[2 * pr][e], r[2 * pr + 1][e]);
+          const float2 delta = add_x2(v, make_float2(-mean2[pr].x, -mean2[pr].y));
+          mean2[pr] = fma_x2(delta, make_float2(inv, inv), mean2[pr]);
+          m2_2[pr] = fma_x2(delta, add_x2(v, make_float2(-mean2[pr].x, -mean2[pr].y)), m2_2[pr]);
+        }
+      } else {  // only the pair's first virtual thread has this group
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float inv = 1.f / static_cast<float>(4 * k + e + 1);
+          const WelfordState st = welford_add(WelfordState{mean2[pr].x, m2_2[pr].x, 0.f},
+                                              r[2 * pr][e], inv);
+          mean2[pr].x = st.mean;
+          m2_2[pr].x = st.m2;
+        }
+      }
+    }
+  }
+  WelfordState st[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    // elements this virtual thread folded: 4 per group with lane + 32w + 128k < n_quads
+    const int first = lane + 32 * w;
+    const int groups = first < n_quads ? min(QPV, (n_quads - first + kAtenThreads - 1) / kAtenThreads) : 0;
+    const float2 m = mean2[w >> 1], q = m2_2[w >> 1];
+    st[w] = WelfordState{(w & 1) ? m.y : m.x, (w & 1) ? q.y : q.x, static_cast<float>(4 * groups)};
   }
   const WelfordState root = welford_tree(st, lane);
   const float mean = __shfl_sync(0xFFFFFFFFu, root.mean, 0);
@@ -485,9 +542,15 @@ __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(co
   const float rstd = rsqrtf(__fadd_rn(var, a.eps));
   const Raw* wq = static_cast<const Raw*>(a.weight);
   const Raw* bq = static_cast<const Raw*>(a.bias);
+  if (zero_norm) {
+    float z[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int qi = lane; qi < n_quads; qi += 32) nq[qi] = Q::pack(z);
+    return;
+  }
   // the second pass reads the rounded residual back (residual_out, or x
   // itself for a plain LayerNorm) unless the row is held in registers
   const Raw* src = has_update ? static_cast<const Raw*>(rq) : xq;
+  const float2 mean_x2 = make_float2(-mean, -mean), rstd_x2 = make_float2(rstd, rstd);
 #pragma unroll
   for (int k = 0; k < QPV; ++k) {
 #pragma unroll
@@ -505,10 +568,14 @@ __global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(co
       Q::unpack(wq[qi], fw);
       if (bq != nullptr) Q::unpack(bq[qi], fb);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float c = __fmul_rn(rstd, __fsub_rn(r[e], mean));
-        const float nrm = bq != nullptr ? __fmaf_rn(fw[e], c, fb[e]) : __fmul_rn(fw[e], c);
-        o[e] = zero_norm ? 0.f : (tf32 ? round_tf32(nrm) : nrm);
+      for (int e = 0; e < 4; e += 2) {
+        // n = w * (rstd * (r - mean)) + b, two elements per instruction
+        const float2 c = mul_x2(rstd_x2, add_x2(make_float2(r[e], r[e + 1]), mean_x2));
+        const float2 n = bq != nullptr ? fma_x2(make_float2(fw[e], fw[e + 1]), c,
+                                                make_float2(fb[e], fb[e + 1]))
+                                       : mul_x2(make_float2(fw[e], fw[e + 1]), c);
+        o[e] = tf32 ? round_tf32(n.x) : n.x;
+        o[e + 1] = tf32 ? round_tf32(n.y) : n.y;
       }
       nq[qi] = Q::pack(o);
     }
