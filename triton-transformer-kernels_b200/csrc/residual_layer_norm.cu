@@ -361,67 +361,39 @@ struct Quad {  // 4 consecutive elements: 16 bytes (fp32) or 8 bytes (16-bit)
   }
 };
 
-// ATen's kernel uses 128 threads per row; here one warp computes a row, lane
-// l standing in for those threads l, l + 32, l + 64 and l + 96 ("virtual
-// threads" 32w + l, w = 0..3 being ATen's warp): each keeps its own Welford
-// state over exactly the elements that ATen thread folds. The combination is
-// the same binary tree as ATen's -- per ATen warp w the shuffle-down levels
-// N16[w][l] = C(leaf[w][l], leaf[w][l + 16]), N8 = C(N16[l], N16[l + 8]), ...,
-// N1[w]; then C(N1[0], N1[2]), C(N1[1], N1[3]) and their combination, C(own,
-// other) with "own" the lower index -- with its nodes spread over the lanes
-// (2 + 1 + 1 + 1 + 1 + 2 combinations per lane instead of 4 per shuffle level)
-// because a combination costs a correctly rounded reciprocal. 8 rows per
-// 256-thread CTA; no shared memory and no block barrier. Rows of at most 1024
-// elements stay in registers between the passes; longer ones are re-read
-// (L2-resident).
+// ATen's kernel uses 128 threads per row; here one warp computes TWO rows,
+// lane l standing in for those threads l, l + 32, l + 64 and l + 96 ("virtual
+// threads" 32w + l, w = 0..3 being ATen's warp) of both rows. Each virtual
+// thread keeps its own Welford state over exactly the elements that ATen
+// thread folds; the two rows' states sit in the halves of f32x2 registers,
+// so every fold and every combination below is one paired instruction for
+// both rows (each half rounded exactly like the scalar operation). The
+// combination is ATen's binary tree -- per ATen warp w the shuffle-down
+// levels N16[w][l] = C(leaf[w][l], leaf[w][l + 16]), N8 = C(N16[l],
+// N16[l + 8]), ..., N1[w]; then C(N1[0], N1[2]), C(N1[1], N1[3]) and their
+// combination, C(own, other) with "own" the lower index -- with its nodes
+// spread over the lanes (2 + 1 + 1 + 1 + 1 + 2 combinations per lane). The
+// element counts depend only on the width and the lane, so the reciprocal of
+// each node's count is shared by the two rows. 8 warps (16 rows) per CTA; no
+// shared memory and no block barrier. Rows of at most 1024 elements stay in
+// registers between the passes; longer ones are re-read (L2-resident).
 constexpr int kAtenThreads = 128;  // ATen's threads per row (4 warps)
-constexpr int kWelfordRowsPerCta = 8;
+constexpr int kWelfordWarpsPerCta = 8;
 
-__device__ __forceinline__ WelfordState shfl_state(const WelfordState& v, int src) {
-  return {__shfl_sync(0xFFFFFFFFu, v.mean, src), __shfl_sync(0xFFFFFFFFu, v.m2, src),
-          __shfl_sync(0xFFFFFFFFu, v.count, src)};
-}
-__device__ __forceinline__ WelfordState shfl_xor_state(const WelfordState& v, int mask) {
-  return {__shfl_xor_sync(0xFFFFFFFFu, v.mean, mask), __shfl_xor_sync(0xFFFFFFFFu, v.m2, mask),
-          __shfl_xor_sync(0xFFFFFFFFu, v.count, mask)};
-}
-__device__ __forceinline__ WelfordState shfl_down_state(const WelfordState& v, int off) {
-  return {__shfl_down_sync(0xFFFFFFFFu, v.mean, off), __shfl_down_sync(0xFFFFFFFFu, v.m2, off),
-          __shfl_down_sync(0xFFFFFFFFu, v.count, off)};
-}
-
-// The root of ATen's combination tree over the 128 virtual-thread states
-// leaf[w] (this lane's virtual threads 32w + lane); valid in lane 0.
-__device__ __forceinline__ WelfordState welford_tree(const WelfordState (&leaf)[4], int lane) {
-  // N16: lane j < 16 builds (w = 0, 2; l = j), lane j >= 16 (w = 1, 3; l = j - 16).
-  // The partner lane j ^ 16 holds the other leaf of each pair.
-  const bool lo = lane < 16;
-  const WelfordState ra = shfl_xor_state(lo ? leaf[1] : leaf[0], 16);
-  const WelfordState rb = shfl_xor_state(lo ? leaf[3] : leaf[2], 16);
-  const WelfordState x = lo ? welford_combine(leaf[0], ra) : welford_combine(ra, leaf[1]);
-  const WelfordState y = lo ? welford_combine(leaf[2], rb) : welford_combine(rb, leaf[3]);
-  // N8[w][l] (l < 8) in lane 8w + l: N16[w][l] and N16[w][l + 8] sit in lanes
-  // l + 16 (w & 1) and l + 8 + 16 (w & 1), in x for w < 2 and y for w >= 2.
-  const int w = lane >> 3, l = lane & 7;
-  const int s1 = l + 16 * (w & 1), s2 = s1 + 8;
-  const WelfordState x1 = shfl_state(x, s1), x2 = shfl_state(x, s2);
-  const WelfordState y1 = shfl_state(y, s1), y2 = shfl_state(y, s2);
-  WelfordState n = w < 2 ? welford_combine(x1, x2) : welford_combine(y1, y2);
-  // N4, N2, N1 within each group of 8 lanes (lane 8w holds N1[w])
-#pragma unroll
-  for (int off = 4; off > 0; off >>= 1) n = welford_combine(n, shfl_down_state(n, off));
-  // C(N1[0], N1[2]) in lane 0, C(N1[1], N1[3]) in lane 8, then C(that, that)
-  n = welford_combine(n, shfl_down_state(n, 16));
-  return welford_combine(n, shfl_down_state(n, 8));
-}
-
-// Two fp32 values per instruction (sm_100 f32x2): each lane of the pair is
-// rounded exactly as the scalar operation, so paired arithmetic is bit-for-bit
-// the scalar arithmetic on each half.
+// Two fp32 values per instruction (sm_100 f32x2): each half is rounded exactly
+// as the scalar operation.
 __device__ __forceinline__ float2 add_x2(float2 a, float2 b) {
   float2 d;
   asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
       "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub_x2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "sub.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
       : "=f"(d.x), "=f"(d.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
@@ -442,142 +414,210 @@ __device__ __forceinline__ float2 fma_x2(float2 a, float2 b, float2 c) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
   return d;
 }
+__device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
+
+// Welford states of one virtual thread for the warp's two rows (count shared).
+struct PairState {
+  float2 mean, m2;
+  float count;
+};
+
+// own (b) folded with other (a), both rows at once; ATen's formula per half.
+__device__ __forceinline__ PairState pair_combine(const PairState& b, const PairState& a) {
+  const float count = __fadd_rn(a.count, b.count);
+  if (!(count > 0.f)) return {splat(0.f), splat(0.f), count};
+  const float coef = __frcp_rn(count);
+  const float na = __fmul_rn(a.count, coef), nb = __fmul_rn(b.count, coef);
+  const float2 delta = sub_x2(b.mean, a.mean);
+  const float2 mean = fma_x2(splat(na), a.mean, mul_x2(splat(nb), b.mean));
+  const float2 m2 = fma_x2(mul_x2(mul_x2(delta, delta), splat(a.count)), splat(nb),
+                           add_x2(a.m2, b.m2));
+  return {mean, m2, count};
+}
+
+__device__ __forceinline__ PairState shfl_pair(const PairState& v, int src) {
+  return {make_float2(__shfl_sync(0xFFFFFFFFu, v.mean.x, src),
+                      __shfl_sync(0xFFFFFFFFu, v.mean.y, src)),
+          make_float2(__shfl_sync(0xFFFFFFFFu, v.m2.x, src), __shfl_sync(0xFFFFFFFFu, v.m2.y, src)),
+          __shfl_sync(0xFFFFFFFFu, v.count, src)};
+}
+__device__ __forceinline__ PairState shfl_xor_pair(const PairState& v, int mask) {
+  return {make_float2(__shfl_xor_sync(0xFFFFFFFFu, v.mean.x, mask),
+                      __shfl_xor_sync(0xFFFFFFFFu, v.mean.y, mask)),
+          make_float2(__shfl_xor_sync(0xFFFFFFFFu, v.m2.x, mask),
+                      __shfl_xor_sync(0xFFFFFFFFu, v.m2.y, mask)),
+          __shfl_xor_sync(0xFFFFFFFFu, v.count, mask)};
+}
+__device__ __forceinline__ PairState shfl_down_pair(const PairState& v, int off) {
+  return {make_float2(__shfl_down_sync(0xFFFFFFFFu, v.mean.x, off),
+                      __shfl_down_sync(0xFFFFFFFFu, v.mean.y, off)),
+          make_float2(__shfl_down_sync(0xFFFFFFFFu, v.m2.x, off),
+                      __shfl_down_sync(0xFFFFFFFFu, v.m2.y, off)),
+          __shfl_down_sync(0xFFFFFFFFu, v.count, off)};
+}
+
+// The root of ATen's combination tree over the 128 virtual-thread states
+// leaf[w] (this lane's virtual threads 32w + lane), for both rows; valid in
+// lane 0.
+__device__ __forceinline__ PairState pair_tree(const PairState (&leaf)[4], int lane) {
+  // N16: lane j < 16 builds (w = 0, 2; l = j), lane j >= 16 (w = 1, 3; l = j - 16);
+  // the partner lane j ^ 16 holds the other leaf of each pair.
+  const bool lo = lane < 16;
+  const PairState ra = shfl_xor_pair(lo ? leaf[1] : leaf[0], 16);
+  const PairState rb = shfl_xor_pair(lo ? leaf[3] : leaf[2], 16);
+  const PairState x = lo ? pair_combine(leaf[0], ra) : pair_combine(ra, leaf[1]);
+  const PairState y = lo ? pair_combine(leaf[2], rb) : pair_combine(rb, leaf[3]);
+  // N8[w][l] (l < 8) in lane 8w + l: N16[w][l] and N16[w][l + 8] sit in lanes
+  // l + 16 (w & 1) and l + 8 + 16 (w & 1), in x for w < 2 and y for w >= 2.
+  const int w = lane >> 3, l = lane & 7;
+  const int s1 = l + 16 * (w & 1), s2 = s1 + 8;
+  const PairState x1 = shfl_pair(x, s1), x2 = shfl_pair(x, s2);
+  const PairState y1 = shfl_pair(y, s1), y2 = shfl_pair(y, s2);
+  PairState n = w < 2 ? pair_combine(x1, x2) : pair_combine(y1, y2);
+  // N4, N2, N1 within each group of 8 lanes (lane 8w holds N1[w])
+#pragma unroll
+  for (int off = 4; off > 0; off >>= 1) n = pair_combine(n, shfl_down_pair(n, off));
+  // C(N1[0], N1[2]) in lane 0, C(N1[1], N1[3]) in lane 8, then C(that, that)
+  n = pair_combine(n, shfl_down_pair(n, 16));
+  return pair_combine(n, shfl_down_pair(n, 8));
+}
 
 template <typename T, int QPV>  // QPV: 4-element groups per ATen thread (width <= 512 * QPV)
-__global__ void __launch_bounds__(32 * kWelfordRowsPerCta) rln_welford_kernel(const RlnArgs a) {
+__global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(const RlnArgs a) {
   using Q = Quad<T>;
   using Raw = typename Q::Raw;
-  constexpr bool kHold = QPV <= 2;  // keep the row in registers between the passes
+  constexpr bool kHold = QPV <= 2;  // keep the rows in registers between the passes
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWelfordRowsPerCta + (threadIdx.x >> 5);
-  if (row >= a.rows) return;  // whole warps leave together
+  const int64_t row0 = 2 * (static_cast<int64_t>(blockIdx.x) * kWelfordWarpsPerCta + (threadIdx.x >> 5));
+  if (row0 >= a.rows) return;  // whole warps leave together
+  // the second row; a last odd row is computed twice and stored once
+  const bool two = row0 + 1 < a.rows;
+  const int64_t rows[2] = {row0, two ? row0 + 1 : row0};
   const int n_quads = static_cast<int>(a.width / 4);
   const bool has_update = !(a.flags & B200TK_RLN_NO_UPDATE);
-  bool valid = true;
-  if (a.mask != nullptr) valid = a.mask[row] != 0;
-  const bool zero_res = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_RESIDUAL);
-  const bool zero_norm = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_NORMALIZED);
+  bool zero_res[2], zero_norm[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool valid = a.mask == nullptr || a.mask[rows[i]] != 0;
+    zero_res[i] = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_RESIDUAL);
+    zero_norm[i] = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_NORMALIZED);
+  }
   const bool tf32 = std::is_same_v<T, float> && (a.flags & B200TK_RLN_ROUND_TF32);
-  const Raw* xq = reinterpret_cast<const Raw*>(static_cast<const T*>(a.x) + row * a.width);
-  const Raw* uq = reinterpret_cast<const Raw*>(static_cast<const T*>(a.update) + row * a.width);
-  Raw* rq = reinterpret_cast<Raw*>(static_cast<T*>(a.residual_out) + row * a.width);
-  Raw* nq = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + row * a.width);
+  const Raw* xq[2];
+  const Raw* uq[2];
+  Raw* rq[2];
+  Raw* nq[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    xq[i] = reinterpret_cast<const Raw*>(static_cast<const T*>(a.x) + rows[i] * a.width);
+    uq[i] = reinterpret_cast<const Raw*>(static_cast<const T*>(a.update) + rows[i] * a.width);
+    rq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.residual_out) + rows[i] * a.width);
+    nq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + rows[i] * a.width);
+  }
 
-  float held[kHold ? QPV * 4 * 4 : 1];
-  // Welford states of the virtual threads w = 0..3 as two pairs (w = 2p, 2p + 1)
-  // updated together with f32x2 arithmetic; the element counts are known.
-  float2 mean2[2] = {{0.f, 0.f}, {0.f, 0.f}}, m2_2[2] = {{0.f, 0.f}, {0.f, 0.f}};
+  float2 held[kHold ? QPV * 4 * 4 : 1];  // (row 0, row 1) of each held element
+  PairState st[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) st[w] = PairState{splat(0.f), splat(0.f), 0.f};
 #pragma unroll
   for (int k = 0; k < QPV; ++k) {
-    // this step's group of every virtual thread, loaded before any is folded
-    Raw xv[4], uv[4];
+    // this step's group of every virtual thread of both rows, loaded first
+    Raw xv[2][4], uv[2][4];
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const int qi = lane + 32 * w + kAtenThreads * k;
       const bool in = qi < n_quads;
-      xv[w] = in ? xq[qi] : Raw{};
-      uv[w] = (in && has_update) ? uq[qi] : Raw{};
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        xv[i][w] = in ? xq[i][qi] : Raw{};
+        uv[i][w] = (in && has_update) ? uq[i][qi] : Raw{};
+      }
     }
-    float r[4][4];
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      Q::unpack(xv[w], r[w]);
-      if (has_update) {
-        float fu[4];
-        Q::unpack(uv[w], fu);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float v = r[w][e] + fu[e];
-          if constexpr (!std::is_same_v<T, float>) v = round_t<T>(v);
-          r[w][e] = v;
-        }
-      }
-      if (zero_res) r[w][0] = r[w][1] = r[w][2] = r[w][3] = 0.f;
       const int qi = lane + 32 * w + kAtenThreads * k;
-      if (has_update && qi < n_quads) rq[qi] = Q::pack(r[w]);
-      if constexpr (kHold) {
+      if (qi >= n_quads) continue;
+      float r[2][4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) held[(k * 4 + w) * 4 + e] = r[w][e];
-      }
-    }
-    // fold: the count before element e of group k is 4k + e, so 1 / (4k + e
-    // + 1) folds to a correctly rounded constant
+      for (int i = 0; i < 2; ++i) {
+        Q::unpack(xv[i][w], r[i]);
+        if (has_update) {
+          float fu[4];
+          Q::unpack(uv[i][w], fu);
 #pragma unroll
-    for (int pr = 0; pr < 2; ++pr) {
-      const int q0 = lane + 32 * (2 * pr) + kAtenThreads * k;  // the pair's first group
-      if (q0 >= n_quads) continue;
-      if (q0 + 32 < n_quads) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float inv = 1.f / static_cast<float>(4 * k + e + 1);
-          const float2 v = make_float2(r[2 * pr][e], r[2 * pr + 1][e]);
-          const float2 delta = add_x2(v, make_float2(-mean2[pr].x, -mean2[pr].y));
-          mean2[pr] = fma_x2(delta, make_float2(inv, inv), mean2[pr]);
-          m2_2[pr] = fma_x2(delta, add_x2(v, make_float2(-mean2[pr].x, -mean2[pr].y)), m2_2[pr]);
-        }
-      } else {  // only the pair's first virtual thread has this group
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float inv = 1.f / static_cast<float>(4 * k + e + 1);
-          const WelfordState st = welford_add(WelfordState{mean2[pr].x, m2_2[pr].x, 0.f},
-                                              r[2 * pr][e], inv);
-          mean2[pr].x = st.mean;
-          m2_2[pr].x = st.m2;
+          for (int e = 0; e < 4; ++e) {
+            float v = r[i][e] + fu[e];
+            if constexpr (!std::is_same_v<T, float>) v = round_t<T>(v);
+            r[i][e] = v;
+          }
+          if (zero_res[i]) r[i][0] = r[i][1] = r[i][2] = r[i][3] = 0.f;
+          if (i == 0 || two) rq[i][qi] = Q::pack(r[i]);
+        } else if (zero_res[i]) {
+          r[i][0] = r[i][1] = r[i][2] = r[i][3] = 0.f;
         }
       }
+      // fold: the count before element e of group k is 4k + e, so
+      // 1 / (4k + e + 1) folds to a correctly rounded constant
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 v = make_float2(r[0][e], r[1][e]);
+        const float2 delta = sub_x2(v, st[w].mean);
+        st[w].mean = fma_x2(delta, splat(1.f / static_cast<float>(4 * k + e + 1)), st[w].mean);
+        st[w].m2 = fma_x2(delta, sub_x2(v, st[w].mean), st[w].m2);
+        if constexpr (kHold) held[(k * 4 + w) * 4 + e] = v;
+      }
+      st[w].count = static_cast<float>(4 * (k + 1));
     }
   }
-  WelfordState st[4];
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    // elements this virtual thread folded: 4 per group with lane + 32w + 128k < n_quads
-    const int first = lane + 32 * w;
-    const int groups = first < n_quads ? min(QPV, (n_quads - first + kAtenThreads - 1) / kAtenThreads) : 0;
-    const float2 m = mean2[w >> 1], q = m2_2[w >> 1];
-    st[w] = WelfordState{(w & 1) ? m.y : m.x, (w & 1) ? q.y : q.x, static_cast<float>(4 * groups)};
-  }
-  const WelfordState root = welford_tree(st, lane);
-  const float mean = __shfl_sync(0xFFFFFFFFu, root.mean, 0);
-  const float var = __fdiv_rn(__shfl_sync(0xFFFFFFFFu, root.m2, 0), static_cast<float>(a.width));
-  const float rstd = rsqrtf(__fadd_rn(var, a.eps));
+  const PairState root = pair_tree(st, lane);
+  float2 mean = make_float2(__shfl_sync(0xFFFFFFFFu, root.mean.x, 0),
+                            __shfl_sync(0xFFFFFFFFu, root.mean.y, 0));
+  const float2 m2 = make_float2(__shfl_sync(0xFFFFFFFFu, root.m2.x, 0),
+                                __shfl_sync(0xFFFFFFFFu, root.m2.y, 0));
+  const float width = static_cast<float>(a.width);
+  const float2 rstd = make_float2(rsqrtf(__fadd_rn(__fdiv_rn(m2.x, width), a.eps)),
+                                  rsqrtf(__fadd_rn(__fdiv_rn(m2.y, width), a.eps)));
   const Raw* wq = static_cast<const Raw*>(a.weight);
   const Raw* bq = static_cast<const Raw*>(a.bias);
-  if (zero_norm) {
-    float z[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int qi = lane; qi < n_quads; qi += 32) nq[qi] = Q::pack(z);
-    return;
-  }
   // the second pass reads the rounded residual back (residual_out, or x
-  // itself for a plain LayerNorm) unless the row is held in registers
-  const Raw* src = has_update ? static_cast<const Raw*>(rq) : xq;
-  const float2 mean_x2 = make_float2(-mean, -mean), rstd_x2 = make_float2(rstd, rstd);
+  // itself for a plain LayerNorm) unless the rows are held in registers
+  const Raw* src[2] = {has_update ? static_cast<const Raw*>(rq[0]) : xq[0],
+                       has_update ? static_cast<const Raw*>(rq[1]) : xq[1]};
 #pragma unroll
   for (int k = 0; k < QPV; ++k) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const int qi = lane + 32 * w + kAtenThreads * k;
       if (qi >= n_quads) continue;
-      float r[4], fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f}, o[4];
+      float2 r[4];
       if constexpr (kHold) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) r[e] = held[(k * 4 + w) * 4 + e];
       } else {
-        Q::unpack(src[qi], r);
-        if (zero_res) r[0] = r[1] = r[2] = r[3] = 0.f;
+        float r0[4], r1[4];
+        Q::unpack(src[0][qi], r0);
+        Q::unpack(src[1][qi], r1);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          r[e] = make_float2(zero_res[0] ? 0.f : r0[e], zero_res[1] ? 0.f : r1[e]);
       }
+      float fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f};
       Q::unpack(wq[qi], fw);
       if (bq != nullptr) Q::unpack(bq[qi], fb);
+      float o[2][4];
 #pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        // n = w * (rstd * (r - mean)) + b, two elements per instruction
-        const float2 c = mul_x2(rstd_x2, add_x2(make_float2(r[e], r[e + 1]), mean_x2));
-        const float2 n = bq != nullptr ? fma_x2(make_float2(fw[e], fw[e + 1]), c,
-                                                make_float2(fb[e], fb[e + 1]))
-                                       : mul_x2(make_float2(fw[e], fw[e + 1]), c);
-        o[e] = tf32 ? round_tf32(n.x) : n.x;
-        o[e + 1] = tf32 ? round_tf32(n.y) : n.y;
+      for (int e = 0; e < 4; ++e) {
+        // n = w * (rstd * (r - mean)) + b, both rows per instruction
+        const float2 c = mul_x2(rstd, sub_x2(r[e], mean));
+        const float2 n = bq != nullptr ? fma_x2(splat(fw[e]), c, splat(fb[e]))
+                                       : mul_x2(splat(fw[e]), c);
+        o[0][e] = tf32 ? round_tf32(n.x) : n.x;
+        o[1][e] = tf32 ? round_tf32(n.y) : n.y;
       }
-      nq[qi] = Q::pack(o);
+      if (zero_norm[0]) o[0][0] = o[0][1] = o[0][2] = o[0][3] = 0.f;
+      if (zero_norm[1]) o[1][0] = o[1][1] = o[1][2] = o[1][3] = 0.f;
+      nq[0][qi] = Q::pack(o[0]);
+      if (two) nq[1][qi] = Q::pack(o[1]);
     }
   }
 }
@@ -586,10 +626,11 @@ template <typename T>
 cudaError_t launch_welford(const RlnArgs& a, cudaStream_t stream) {
   const int64_t quads = a.width / 4;
   const int qpv = static_cast<int>((quads + kAtenThreads - 1) / kAtenThreads);
-  const int64_t grid = (a.rows + kWelfordRowsPerCta - 1) / kWelfordRowsPerCta;
+  constexpr int kRowsPerCta = 2 * kWelfordWarpsPerCta;
+  const int64_t grid = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
   if (grid > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
   const unsigned g = static_cast<unsigned>(grid);
-  constexpr int kBlock = 32 * kWelfordRowsPerCta;
+  constexpr int kBlock = 32 * kWelfordWarpsPerCta;
   switch (qpv) {
     case 1: rln_welford_kernel<T, 1><<<g, kBlock, 0, stream>>>(a); break;
     case 2: rln_welford_kernel<T, 2><<<g, kBlock, 0, stream>>>(a); break;

@@ -16,21 +16,19 @@ path, submission.py:674-723). Up to GRAPH_CACHE_SIZE captures are kept.
 On an sm_100 GPU in inference mode every layer runs
   packed QKV projection (cuBLAS, one GEMM)
   -> fused attention (libb200tk, tcgen05)
-  -> out_proj + residual (16-bit: libb200tk, one tcgen05 GEMM with the
-     residual add in its epilogue, then LayerNorm norm2; fp32: cuBLAS, then
-     the fused residual + norm2 kernel)
+  -> out_proj (cuBLAS) -> fused residual + norm2 (libb200tk)
   -> ffn_in + exact GELU (libb200tk, one tcgen05 GEMM with the GELU in its
      epilogue)
-  -> ffn_out + residual + next norm1 / final_norm (as for out_proj)
+  -> ffn_out (cuBLAS) -> fused residual + next norm1 / final_norm (libb200tk)
 which is the reference's fused layer loop (:481-525) applied to every shape
 and dtype instead of four measured rows. ffn_backend ("auto" | "b200" |
 "torch") picks the FFN input projection: the fused kernel ("auto": where it
 applies and the output has at least FUSED_FFN_MIN_OUTPUTS elements; fp32
 only while TF32 matmuls are allowed, the precision the unfused fp32 Linear
 then has), or cuBLAS + ATen GELU. residual_backend (same values) picks
-out_proj / ffn_out: GEMMs with the residual add in their epilogue followed
-by plain LayerNorms ("auto": 16-bit models), or cuBLAS + the fused residual
-LayerNorm. attention_schedule ("auto" | "two_pass" | "one_pass") is the
+out_proj / ffn_out: "b200" runs them as GEMMs with the residual add in their
+epilogue followed by plain LayerNorms; "auto" / "torch" keep cuBLAS + the
+fused residual LayerNorm (faster at the BASELINE shapes). attention_schedule ("auto" | "two_pass" | "one_pass") is the
 16-bit softmax schedule of the attention kernel (see attention_forward).
 Everything else (CPU, autograd,
 training mode, backends other than the custom one) runs the explicit
@@ -723,16 +721,17 @@ class UserOptimizedTransformer(TransformerWeights):
 
     def _residual_fused(self, x: torch.Tensor) -> bool:
         """Whether out_proj and ffn_out run as GEMMs with the residual add in
-        their epilogue, for a block whose residual stream is like x. "auto"
-        fuses 16-bit models from FUSED_FFN_MIN_OUTPUTS outputs per projection
-        on; fp32 only when forced (and with TF32 matmuls allowed): an fp32
-        Linear under the harness flags multiplies TF32 operands rounded to
-        nearest, while the kernel truncates the operands it reads."""
-        if self.residual_backend == "torch":
+        their epilogue, for a block whose residual stream is like x. Only when
+        forced (residual_backend="b200"): at the BASELINE shapes cuBLAS's
+        GEMM plus the fused residual LayerNorm is faster than this library's
+        GEMM with the add in its epilogue (measured: C5 out_proj 0.24 vs 0.40
+        ms, ffn_out 0.83 vs 0.98 ms; C3 1.35 vs 1.61, 6.03 vs 7.38 ms), so
+        "auto" keeps cuBLAS. fp32 additionally needs TF32 matmuls allowed: an
+        fp32 Linear under the harness flags multiplies TF32 operands rounded
+        to nearest, while the kernel truncates the operands it reads."""
+        if self.residual_backend in ("torch", "auto"):
             return False
-        if x.dtype == torch.float32 and (
-            self.residual_backend == "auto" or not torch.backends.cuda.matmul.allow_tf32
-        ):
+        if x.dtype == torch.float32 and not torch.backends.cuda.matmul.allow_tf32:
             return False
         layer = self.layers[0]
         for linear in (layer.attention.out_proj, layer.ffn_out):
@@ -741,8 +740,7 @@ class UserOptimizedTransformer(TransformerWeights):
                 if self.residual_backend == "b200":
                     raise ValueError(f"residual_backend='b200' cannot run this block: {reason}")
                 return False
-        outputs = x.numel()  # rows x d_model per projection
-        return self.residual_backend == "b200" or outputs >= FUSED_FFN_MIN_OUTPUTS
+        return True
 
     def _fused_block(
         self,
