@@ -487,6 +487,9 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
   using Q = Quad<T>;
   using Raw = typename Q::Raw;
   constexpr bool kHold = QPV <= 2;  // keep the rows in registers between the passes
+  // 16-bit held rows also take their weight / bias groups early (fp32 rows
+  // would need twice the registers)
+  constexpr bool kPrefetch = kHold && !std::is_same_v<T, float>;
   const int lane = threadIdx.x & 31;
   const int64_t row0 = 2 * (static_cast<int64_t>(blockIdx.x) * kWelfordWarpsPerCta + (threadIdx.x >> 5));
   if (row0 >= a.rows) return;  // whole warps leave together
@@ -515,7 +518,7 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
     nq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + rows[i] * a.width);
   }
 
-  float2 held[kHold ? QPV * 4 * 4 : 1];  // (row 0, row 1) of each held element
+  Raw held[kHold ? QPV * 4 : 1][2];  // the rounded residual groups of both rows, packed
   PairState st[4];
 #pragma unroll
   for (int w = 0; w < 4; ++w) st[w] = PairState{splat(0.f), splat(0.f), 0.f};
@@ -556,6 +559,11 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
           r[i][0] = r[i][1] = r[i][2] = r[i][3] = 0.f;
         }
       }
+      if constexpr (kHold) {
+        // r is a T value (rounded residual, or x itself): packing is exact
+        held[k * 4 + w][0] = Q::pack(r[0]);
+        held[k * 4 + w][1] = Q::pack(r[1]);
+      }
       // fold: the count before element e of group k is 4k + e, so
       // 1 / (4k + e + 1) folds to a correctly rounded constant
 #pragma unroll
@@ -564,9 +572,21 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
         const float2 delta = sub_x2(v, st[w].mean);
         st[w].mean = fma_x2(delta, splat(1.f / static_cast<float>(4 * k + e + 1)), st[w].mean);
         st[w].m2 = fma_x2(delta, sub_x2(v, st[w].mean), st[w].m2);
-        if constexpr (kHold) held[(k * 4 + w) * 4 + e] = v;
       }
       st[w].count = static_cast<float>(4 * (k + 1));
+    }
+  }
+  // weight / bias groups of this lane, requested before the combination
+  // tree so that their (L2) latency overlaps it
+  const Raw* wq = static_cast<const Raw*>(a.weight);
+  const Raw* bq = static_cast<const Raw*>(a.bias);
+  Raw wv[kPrefetch ? QPV * 4 : 1], bv[kPrefetch ? QPV * 4 : 1];
+  if constexpr (kPrefetch) {
+#pragma unroll
+    for (int g = 0; g < QPV * 4; ++g) {
+      const int qi = lane + 32 * (g & 3) + kAtenThreads * (g >> 2);
+      wv[g] = qi < n_quads ? wq[qi] : Raw{};
+      bv[g] = (qi < n_quads && bq != nullptr) ? bq[qi] : Raw{};
     }
   }
   const PairState root = pair_tree(st, lane);
@@ -577,8 +597,6 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
   const float width = static_cast<float>(a.width);
   const float2 rstd = make_float2(rsqrtf(__fadd_rn(__fdiv_rn(m2.x, width), a.eps)),
                                   rsqrtf(__fadd_rn(__fdiv_rn(m2.y, width), a.eps)));
-  const Raw* wq = static_cast<const Raw*>(a.weight);
-  const Raw* bq = static_cast<const Raw*>(a.bias);
   // the second pass reads the rounded residual back (residual_out, or x
   // itself for a plain LayerNorm) unless the rows are held in registers
   const Raw* src[2] = {has_update ? static_cast<const Raw*>(rq[0]) : xq[0],
@@ -590,9 +608,13 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
       const int qi = lane + 32 * w + kAtenThreads * k;
       if (qi >= n_quads) continue;
       float2 r[4];
+      float fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f};
       if constexpr (kHold) {
+        float r0[4], r1[4];
+        Q::unpack(held[k * 4 + w][0], r0);
+        Q::unpack(held[k * 4 + w][1], r1);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) r[e] = held[(k * 4 + w) * 4 + e];
+        for (int e = 0; e < 4; ++e) r[e] = make_float2(r0[e], r1[e]);
       } else {
         float r0[4], r1[4];
         Q::unpack(src[0][qi], r0);
@@ -601,9 +623,13 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
         for (int e = 0; e < 4; ++e)
           r[e] = make_float2(zero_res[0] ? 0.f : r0[e], zero_res[1] ? 0.f : r1[e]);
       }
-      float fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f};
-      Q::unpack(wq[qi], fw);
-      if (bq != nullptr) Q::unpack(bq[qi], fb);
+      if constexpr (kPrefetch) {
+        Q::unpack(wv[k * 4 + w], fw);
+        if (bq != nullptr) Q::unpack(bv[k * 4 + w], fb);
+      } else {
+        Q::unpack(wq[qi], fw);
+        if (bq != nullptr) Q::unpack(bq[qi], fb);
+      }
       float o[2][4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
