@@ -750,7 +750,14 @@ def run_b200_arm(args) -> int:
     value = tokens / (ms_per_step / 1000.0)
     flops = attention_flops(b, s, h, d // h, causal)
     achieved_tflops = flops / (attn_ms / 1000.0) / 1e12
-    peak_tf = peaks["bf16_tflops_sustained"]
+    # Roofline denominators: the sustained GEMM rate when the timed step ran
+    # under the power cap (median SM clock below 90% of its maximum), the
+    # burst rate when it ran at full clock (a short step).
+    clock = clocks.summary()
+    capped = bool(clock["sm_mhz"] and clock["sm_max_mhz"]
+                  and clock["sm_mhz"] < 0.9 * clock["sm_max_mhz"])
+    peak_kind = "sustained" if capped else "burst"
+    peak_tf = peaks["bf16_tflops_sustained"] if capped else peaks["bf16_tflops"]
     roofline = {
         "bound": "tensor",
         "kernel": "attention_fwd_tc_kernel",
@@ -758,21 +765,24 @@ def run_b200_arm(args) -> int:
         "peak": peak_tf,
         "unit": "TFLOP/s",
         "frac": achieved_tflops / peak_tf,
-        "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside the step)",
+        "peak_source": (f"{peaks['source']} bf16_tflops_{peak_kind} (median SM clock "
+                        f"{clock['sm_mhz']} of {clock['sm_max_mhz']} MHz in the timed region)"),
         "traffic": ncu_traffic("attention", name, b),
         "flops_per_launch": flops,
         "launch_ms": attn_ms,
     }
+    tf32_peak = None
     if tf32 is not None:
+        tf32_peak = tf32["tf32_tflops_sustained"] if capped else tf32["tf32_tflops"]
         # 3xTF32: three TF32 MMAs per product
-        roofline["note"] = "fp32 runs 3xTF32: tensor ceiling = measured TF32 sustained / 3"
-        roofline["frac_of_3xtf32_ceiling"] = achieved_tflops / (tf32["tf32_tflops_sustained"] / 3.0)
+        roofline["note"] = f"fp32 runs 3xTF32: tensor ceiling = measured TF32 {peak_kind} / 3"
+        roofline["frac_of_3xtf32_ceiling"] = achieved_tflops / (tf32_peak / 3.0)
     if dtype == torch.float32:
-        ffn_peak = tf32["tf32_tflops_sustained"] if tf32 else float("nan")
-        ffn_source = "TF32 cuBLAS GEMM measured in this process, sustained"
+        ffn_peak = tf32_peak if tf32_peak else float("nan")
+        ffn_source = f"TF32 cuBLAS GEMM measured in this process, {peak_kind}"
     else:
-        ffn_peak = peaks["bf16_tflops_sustained"]
-        ffn_source = f"{peaks['source']} bf16_tflops_sustained"
+        ffn_peak = peak_tf
+        ffn_source = f"{peaks['source']} bf16_tflops_{peak_kind}"
     rln_gbs = rln_bytes / (rln_ms / 1000.0) / 1e9
     sizes = [hi - lo for lo, hi in shards]
     line = {
@@ -835,7 +845,7 @@ def run_b200_arm(args) -> int:
         "attention_c3_alone": attention_c3,
         "tf32_peak": tf32,
         "gpu_launches": launches,
-        "clocks": clocks.summary(),
+        "clocks": clock,
         "validation": validation,
         "device_status": [int(r[0]) for r in per_rank],
     }

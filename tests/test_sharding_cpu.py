@@ -66,3 +66,45 @@ def test_two_rank_gather_and_max_over_ranks():
         stats, worst = results[rank]
         assert stats == [[0.0, 5.0], [1.0, 5.0]]
         assert worst == 3.0
+
+
+def _gather_worker(rank, world, port, queue):
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        total = 11  # uneven shards: 6 + 5 sequences
+        full = torch.arange(total * 3 * 4, dtype=torch.float32).view(total, 3, 4)
+        start, stop = shard_range(total, world, rank)
+        indices = bench.sample_indices("C5", total)
+        sample = bench.gather_sample(full[start:stop], start, indices, world, torch.device("cpu"))
+        queue.put((rank, indices, None if sample is None else sample.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_output_sample_gathers_the_global_sequences_to_rank_0():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        rank, indices, sample = queue.get(timeout=120)
+        results[rank] = (indices, sample)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    indices, sample = results[0]
+    full = torch.arange(11 * 3 * 4, dtype=torch.float32).view(11, 3, 4)
+    assert indices == [0, 1, 3, 4, 6, 7, 9, 10]  # 8 spread over 11 sequences
+    assert torch.equal(torch.tensor(sample), full[indices])
+    assert results[1][1] is None  # only rank 0 receives the sample
