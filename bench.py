@@ -71,6 +71,12 @@ VALIDATION_SEQUENCES = {"C1": 2, "C2": 2, "C3": 1, "C4": 2, "C5": 8}
 NCU_TRAFFIC = {
     # fp32 3xTF32 attention, full C2: 201.5 MB read + 48.3 MB written
     ("attention", "C2"): (249.8e6, 8),
+    # bf16 attention, one-pass schedule, C3 at batch 1: 425.9 MB read +
+    # 117.1 MB written
+    ("attention", "C3"): (543.0e6, 1),
+    # bf16 attention, two-pass schedule, C5 at batch 64: 151.1 MB read +
+    # 27.7 MB written (part of the output still in L2 at kernel end)
+    ("attention", "C5"): (178.8e6, 64),
     # fused FFN projection, TF32, full C2: 113.0 MB read + 218.4 MB written
     ("ffn", "C2"): (331.4e6, 8),
     # fused FFN projection, bf16, C5 at batch 128: 105.6 MB read + 344.8 MB
