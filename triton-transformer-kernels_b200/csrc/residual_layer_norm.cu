@@ -14,7 +14,7 @@
 // HBM sees exactly one read of x, update and one write of r, n (the roofline
 // minimum of 4 * width * sizeof(T) bytes per row).
 //
-// Welford path (rows of whole 4-element groups up to 4096 wide): the
+// Welford path (16-bit rows of whole 4-element groups up to 4096 wide): the
 // statistics in the order of ATen's vectorised LayerNorm kernel, so the
 // normalized output equals torch's layer_norm bit for bit (see
 // rln_welford_kernel).
@@ -747,9 +747,13 @@ template <typename T>
 cudaError_t launch_typed(const RlnArgs& a, cudaStream_t stream) {
   constexpr int EPV = VecIO<T>::kEPV;
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  // Rows of whole 4-element groups, up to 4096 wide, take the Welford path
-  // (statistics in ATen's order); wider or unaligned rows the paths below.
-  const bool welford_ok = a.width % 4 == 0 && a.width <= 4 * kAtenThreads * 8 &&
+  // 16-bit rows of whole 4-element groups, up to 4096 wide, take the Welford
+  // path (statistics in ATen's order, so the 16-bit output equals torch's
+  // bit for bit); fp32, wider or unaligned rows the paths below (fp32 output
+  // within ~1e-6 of torch's, where one unit of a 16-bit output is 2^-8 or
+  // 2^-11 relative).
+  const bool welford_ok = !std::is_same_v<T, float> && a.width % 4 == 0 &&
+                          a.width <= 4 * kAtenThreads * 8 &&
                           aligned(a.x) && aligned(a.weight) && aligned(a.normalized_out) &&
                           (a.bias == nullptr || aligned(a.bias)) &&
                           ((a.flags & B200TK_RLN_NO_UPDATE) ||
