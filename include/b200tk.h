@@ -65,11 +65,16 @@ extern "C" {
  * the cost of a second Q K^T and a second exp per score. ONE_PASS is the
  * online softmax: unnormalised probabilities are rounded to the input dtype
  * and the output is divided by the row sum at the end (one Q K^T, one exp).
- * AUTO picks per call (b200tk_attention_fwd). float32 always runs its single
+ * RESIDENT keeps TWO_PASS's rounding boundary with one Q K^T and one exp per
+ * score: the whole score row of a 128-row query tile stays in tensor memory
+ * (float16/bfloat16, head_dim 64, seq_len <= 512, scale > 0 only).
+ * AUTO picks per call (b200tk_attention_fwd): RESIDENT where it applies,
+ * ONE_PASS from seq_len 4096, else TWO_PASS. float32 always runs its single
  * 3xTF32 schedule; the CUDA-core route is always online. */
 #define B200TK_SCHEDULE_AUTO 0
 #define B200TK_SCHEDULE_TWO_PASS 1
 #define B200TK_SCHEDULE_ONE_PASS 2
+#define B200TK_SCHEDULE_RESIDENT 3
 
 /* Attention kernel routes reported by b200tk_attention_route. */
 #define B200TK_ROUTE_TCGEN05 1 /* TMA + tcgen05.mma + TMEM pipeline */
@@ -114,7 +119,8 @@ B200TK_API int b200tk_attention_fwd(const void* q, const int64_t* q_strides, con
  * b200tk_attention_fwd with an explicit softmax schedule for 16-bit inputs
  * (B200TK_SCHEDULE_*; AUTO is b200tk_attention_fwd itself). A schedule
  * outside that set is B200TK_ERR_INVALID_ARGUMENT; ONE_PASS with scale <= 0
- * runs TWO_PASS.
+ * runs TWO_PASS; RESIDENT on arguments outside its envelope (or that leave
+ * the tensor-core route) is B200TK_ERR_UNSUPPORTED.
  *
  * Replaces: the same reference kernel as b200tk_attention_fwd; the schedule
  * choice has no counterpart there (its fp16 kernel is online,

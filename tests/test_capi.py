@@ -152,3 +152,27 @@ def test_work_item_range_is_checked_before_any_launch():
     narrow = (s * h * 32, h * 32, 32)
     assert _route(ptrs, [narrow] * 3, shape=(1 << 20, s, h, 32)) == _native.ERR_UNSUPPORTED
     assert _route(ptrs, [narrow] * 3, shape=(1 << 10, s, h, 32)) == _native.ROUTE_GENERIC
+
+
+def test_attention_schedule_validation_needs_no_gpu():
+    # An unknown schedule is an invalid argument; an explicit RESIDENT request
+    # outside its envelope (head_dim 128, seq_len 513, float32, scale <= 0)
+    # is refused before anything is launched.
+    lib = _native.load()
+    base = 1 << 20
+
+    def call(schedule, dtype=2, shape=(2, 128, 4, 64), scale=0.125):
+        b, s, h, d = shape
+        st = (ctypes.c_int64 * 3)(s * h * d, h * d, d)
+        p = ctypes.c_void_p(base)
+        return lib.b200tk_attention_fwd_scheduled(p, st, p, st, p, st, None, None, p, dtype,
+                                                  b, s, h, d, 0, scale, schedule, None)
+
+    assert call(4) == _native.ERR_INVALID_ARGUMENT
+    assert b"schedule" in lib.b200tk_last_error()
+    for kwargs in ({"shape": (2, 128, 4, 128)}, {"shape": (2, 513, 4, 64)}, {"dtype": 0},
+                   {"scale": -0.125}):
+        assert call(_native.SCHEDULES["resident"], **kwargs) == _native.ERR_UNSUPPORTED
+        assert b"resident schedule" in lib.b200tk_last_error()
+    # zero batch: validated, nothing to launch
+    assert call(_native.SCHEDULES["resident"], shape=(0, 128, 4, 64)) == _native.OK

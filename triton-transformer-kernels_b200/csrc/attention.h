@@ -36,6 +36,11 @@ int attention_tc_block_n(int dtype, int head_dim);
 constexpr int64_t kOnePassMinSeq = 4096;
 // Whether a 16-bit tcgen05 launch takes the one-pass schedule.
 bool attention_tc_one_pass(int dtype, int64_t seq, float scale, int schedule);
+// Whether the arguments are inside the row-resident schedule's envelope
+// (16-bit, head_dim 64, 1 <= seq <= 512, scale > 0), and whether a launch
+// with this schedule request takes it.
+bool attention_tc_resident_fits(int dtype, int64_t head_dim, int64_t seq, float scale);
+bool attention_tc_resident(int dtype, int64_t head_dim, int64_t seq, float scale, int schedule);
 // Whether the tcgen05 kernel's work-item numbering fits in int for this
 // shape: the causal pair schedule numbers 2 * ceil(tiles / 2) items per
 // (batch, head) and looks up to 2 * grid items ahead. Host-only arithmetic.

@@ -1,9 +1,11 @@
 // attention_tc.cu - host-side launcher of the tcgen05 attention kernels
-// (kernel: attention_tc.cuh): fills the kernel parameter block and picks the
-// (dtype, head_dim, causal, mask) instantiation.
+// (kernels: attention_tc.cuh, attention_resident.cuh): fills the kernel
+// parameter block and picks the schedule and the (dtype, head_dim, causal,
+// mask) instantiation.
 #include <atomic>
 #include <cmath>
 
+#include "attention_resident.cuh"
 #include "attention_tc.cuh"
 
 namespace b200tk {
@@ -23,9 +25,21 @@ bool attention_tc_one_pass(int dtype, int64_t seq, float scale, int schedule) {
   return seq >= kOnePassMinSeq;
 }
 
+bool attention_tc_resident_fits(int dtype, int64_t head_dim, int64_t seq, float scale) {
+  return dtype != B200TK_DTYPE_FLOAT32 && head_dim == tc::RrLayout::D && seq >= 1 &&
+         seq <= tc::RrLayout::kMaxSeq && scale > 0.f;
+}
+
+bool attention_tc_resident(int dtype, int64_t head_dim, int64_t seq, float scale, int schedule) {
+  return (schedule == B200TK_SCHEDULE_AUTO || schedule == B200TK_SCHEDULE_RESIDENT) &&
+         attention_tc_resident_fits(dtype, head_dim, seq, scale);
+}
+
 bool attention_tc_items_fit(int dtype, int head_dim, int64_t batch, int64_t seq, int64_t heads) {
+  // The row-resident schedule takes one 128-row query tile per item (the
+  // most items of any schedule for its shapes).
   int nq = 1;
-  if (dtype != B200TK_DTYPE_FLOAT32)
+  if (dtype != B200TK_DTYPE_FLOAT32 && !(head_dim == tc::RrLayout::D && seq <= tc::RrLayout::kMaxSeq))
     nq = head_dim == 128 ? tc::TcTile<__half, 128>::kNQ : tc::TcTile<__half, 64>::kNQ;
   const int64_t rows_per_item = static_cast<int64_t>(nq) * tc::BM;
   const int64_t tiles = (seq + rows_per_item - 1) / rows_per_item;
@@ -73,6 +87,11 @@ cudaError_t launch_attention_tc(const AttnTcArgs& a, cudaStream_t stream) {
     err = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device);
     if (err != cudaSuccess) return err;
     sm_count[device].store(num_sms, std::memory_order_relaxed);
+  }
+  if (attention_tc_resident(a.dtype, a.head_dim, a.seq, a.scale, a.schedule)) {
+    return a.dtype == B200TK_DTYPE_BFLOAT16
+               ? tc::launch_resident<__nv_bfloat16>(prm, num_sms, causal, has_mask, stream)
+               : tc::launch_resident<__half>(prm, num_sms, causal, has_mask, stream);
   }
   switch (a.dtype) {
     case B200TK_DTYPE_BFLOAT16:

@@ -27,6 +27,7 @@ OUTPUT = PKG_ROOT / "transformer_opt" / "kernels" / "libb200tk.so"
 UNITS = [
     ("capi.cu", "capi", ()),
     ("attention_tc.cu", "attention_tc", ()),
+    ("attention_resident.cu", "attention_resident", ()),
     ("attention_generic.cu", "attention_generic", ()),
     ("residual_layer_norm.cu", "residual_layer_norm", ()),
     ("linear_gelu.cu", "linear_gelu", ()),
@@ -40,7 +41,7 @@ UNITS = [
     for hd in (64, 128)
 ]
 SOURCES = tuple(sorted({u[0] for u in UNITS}))
-HEADERS = ("attention.h", "attention_tc.cuh", "ptx_sm100.cuh")
+HEADERS = ("attention.h", "attention_tc.cuh", "attention_resident.cuh", "ptx_sm100.cuh")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 COMMON_FLAGS = (
     "-O3",

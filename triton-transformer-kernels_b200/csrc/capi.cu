@@ -263,7 +263,7 @@ int b200tk_attention_fwd_scheduled(const void* q, const int64_t* q_strides, cons
                                    int64_t head_dim, int causal, float scale, int schedule,
                                    void* stream) {
   if (schedule != B200TK_SCHEDULE_AUTO && schedule != B200TK_SCHEDULE_TWO_PASS &&
-      schedule != B200TK_SCHEDULE_ONE_PASS)
+      schedule != B200TK_SCHEDULE_ONE_PASS && schedule != B200TK_SCHEDULE_RESIDENT)
     return fail(B200TK_ERR_INVALID_ARGUMENT, "unknown attention schedule");
   int rc = validate_attention(q, q_strides, k, k_strides, v, v_strides, dtype, batch, seq_len,
                               heads, head_dim);
@@ -278,6 +278,12 @@ int b200tk_attention_fwd_scheduled(const void* q, const int64_t* q_strides, cons
   if (route == B200TK_ROUTE_TCGEN05 && !aligned16(out)) route = B200TK_ROUTE_GENERIC;
   rc = check_item_range(route, dtype, batch, seq_len, heads, head_dim);
   if (rc != B200TK_OK) return rc;
+  if (schedule == B200TK_SCHEDULE_RESIDENT &&
+      (route != B200TK_ROUTE_TCGEN05 ||
+       !attention_tc_resident_fits(dtype, head_dim, seq_len, scale)))
+    return fail(B200TK_ERR_UNSUPPORTED,
+                "the resident schedule needs float16/bfloat16, head_dim 64, seq_len <= 512, "
+                "scale > 0 and tensor-core-route strides");
   if (route == B200TK_ROUTE_TCGEN05) {
     AttnTcArgs a;
     std::memset(&a, 0, sizeof(a));

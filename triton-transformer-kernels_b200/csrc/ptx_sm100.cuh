@@ -474,6 +474,17 @@ __device__ __forceinline__ void tmem_st16x128b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// 16x128b with 8 repetitions (32 columns): the first half of the x16 form.
+__device__ __forceinline__ void tmem_st16x128b_x8(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x128b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 // Hardware base-2 exponential (MUFU.EX2), flush-to-zero; exp2(-inf) = 0.
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

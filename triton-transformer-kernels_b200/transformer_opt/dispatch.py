@@ -125,7 +125,10 @@ def attention_forward(
     ``schedule`` (not in the reference's signature) picks the softmax
     schedule of 16-bit inputs on the custom route: "two_pass" rounds
     normalised probabilities (the explicit math's rounding), "one_pass" is
-    the online softmax, "auto" takes one pass from 4096 keys on."""
+    the online softmax, "resident" rounds like "two_pass" with whole score
+    rows held on chip (head_dim 64, at most 512 keys); "auto" takes
+    "resident" where it applies, one pass from 4096 keys on, else two
+    passes."""
     _validate_backend(backend)
     support = b200_attention_support(q, k, v, valid_token_mask)
 

@@ -33,7 +33,7 @@ RLN_ROUND_TF32 = 8
 STATUS_PIPELINE_TIMEOUT = 1
 STATUS_SELFTEST_TIMEOUT = 2
 
-SCHEDULES = {"auto": 0, "two_pass": 1, "one_pass": 2}
+SCHEDULES = {"auto": 0, "two_pass": 1, "one_pass": 2, "resident": 3}
 
 ROUTE_TCGEN05 = 1
 ROUTE_GENERIC = 2
@@ -151,7 +151,7 @@ def attention_fwd(
     """Launch fused attention on the current stream of q's device.
 
     ``schedule`` picks the 16-bit softmax schedule ("auto", "two_pass",
-    "one_pass"; see B200TK_SCHEDULE_* in include/b200tk.h)."""
+    "one_pass", "resident"; see B200TK_SCHEDULE_* in include/b200tk.h)."""
     lib = load()
     b, s, h, d = q.shape
     qs, ks, vs = _strides(q.stride()[:3]), _strides(k.stride()[:3]), _strides(v.stride()[:3])

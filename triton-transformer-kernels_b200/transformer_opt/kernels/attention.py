@@ -38,11 +38,15 @@ def b200_attention(
 ) -> torch.Tensor:
     """Run the fused kernel and return a fresh contiguous ``[B, S, H, D]`` tensor.
 
-    ``schedule`` ("auto", "two_pass", "one_pass") picks the softmax schedule
-    of 16-bit inputs on the tensor-core route: two passes round the
-    normalised probabilities to the input dtype (the explicit reference's
-    rounding); one pass rounds them before normalisation and does half the
-    exponentials and two thirds of the MMAs. fp32 has a single schedule."""
+    ``schedule`` ("auto", "two_pass", "one_pass", "resident") picks the
+    softmax schedule of 16-bit inputs on the tensor-core route: two passes
+    round the normalised probabilities to the input dtype (the explicit
+    reference's rounding); one pass rounds them before normalisation and does
+    half the exponentials and two thirds of the MMAs; "resident" (head_dim
+    64, at most 512 keys) keeps whole score rows in tensor memory and rounds
+    like two passes with the work of one. "auto" takes "resident" where it
+    applies, one pass from 4096 keys, else two passes. fp32 has a single
+    schedule."""
     support = b200_attention_support(q, k, v, valid_token_mask)
     if not support.supported:
         raise ValueError(f"unsupported b200 attention input: {support.reason}")

@@ -28,7 +28,7 @@ only while TF32 matmuls are allowed, the precision the unfused fp32 Linear
 then has), or cuBLAS + ATen GELU. residual_backend (same values) picks
 out_proj / ffn_out: "b200" runs them as GEMMs with the residual add in their
 epilogue followed by plain LayerNorms; "auto" / "torch" keep cuBLAS + the
-fused residual LayerNorm (faster at the BASELINE shapes). attention_schedule ("auto" | "two_pass" | "one_pass") is the
+fused residual LayerNorm (faster at the BASELINE shapes). attention_schedule ("auto" | "two_pass" | "one_pass" | "resident") is the
 16-bit softmax schedule of the attention kernel (see attention_forward).
 Everything else (CPU, autograd,
 training mode, backends other than the custom one) runs the explicit
@@ -80,7 +80,7 @@ from transformer_opt.model import (
 EXECUTION_MODES = ("auto", "eager", "graph")
 FFN_BACKENDS = ("auto", "b200", "torch")
 RESIDUAL_BACKENDS = ("auto", "b200", "torch")
-ATTENTION_SCHEDULES = ("auto", "two_pass", "one_pass")
+ATTENTION_SCHEDULES = ("auto", "two_pass", "one_pass", "resident")
 # ffn_backend="auto" fuses the FFN input projection with its GELU when the
 # projection has at least this many output elements (rows * ffn_dim); below
 # it the launch and the CTA-pair set-up outweigh the saved GELU pass.
