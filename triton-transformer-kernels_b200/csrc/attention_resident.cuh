@@ -263,6 +263,7 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
     const bool leader = elect_one_sync();
     constexpr uint32_t kFmt = ElemTraits<T>::kFmt;
     constexpr uint32_t idesc_qk = make_idesc(kFmt, 0, 0, BN, BM);  // Q K-major, K K-major
+    constexpr uint32_t idesc_qk2 = make_idesc(kFmt, 0, 0, 2 * BN, BM);  // two key tiles
     constexpr uint32_t idesc_pv = make_idesc(kFmt, 0, 1, D, BM);   // P (tmem), V MN-major
     const uint64_t q_desc0 = make_sdesc(sbase + L::kQ, 16, 1024, kLayoutSw128);
     const uint64_t k_desc0 = make_sdesc(sbase + L::kK, 16, 1024, kLayoutSw128);
@@ -279,12 +280,20 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
       ok = wait_all(bar_q_full(qs), (k >> 1) & 1);
       if (!ok) break;
       bool o_free = k == 0;
-      // S_j = Q K_j^T into key tile j's columns
-      for (int j = 0; j < w.n_kv && ok; ++j) {
+      // S_j = Q K_j^T into key tile j's columns. Two key tiles in adjacent
+      // ring slots (slot of tile j even) take one N = 256 MMA per K step:
+      // their K rows are contiguous in shared memory and their score columns
+      // in TMEM.
+      for (int j = 0; j < w.n_kv && ok;) {
         const int kg = kc + j;
         const int s = kg % L::KST;
-        ok = wait_all(bar_k_full(s), (kg / L::KST) & 1);
-        if (ok && j == L::kTiles - 1 && !o_free) {
+        const bool wide = (s % 2 == 0) && j + 1 < w.n_kv;
+        const int last = wide ? j + 1 : j;
+        for (int jj = j; jj <= last && ok; ++jj) {
+          const int g = kc + jj;
+          ok = wait_all(bar_k_full(g % L::KST), (g / L::KST) & 1);
+        }
+        if (ok && last == L::kTiles - 1 && !o_free) {
           ok = wait_all(bar_o_empty, (k - 1) & 1);
           o_free = true;
         }
@@ -296,24 +305,30 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks)  // 32 bytes of K per step, one swizzle atom
             mma_ss_f16(tmem + j * BN, qd + static_cast<uint32_t>(ks * 2),
-                       kd + static_cast<uint32_t>(ks * 2), idesc_qk, ks > 0 ? 1u : 0u);
-          tc_commit(bar_k_empty(s));
-          if (j == w.n_kv - 1) tc_commit(bar_q_empty(qs));
-          tc_commit(bar_s_full(j));
+                       kd + static_cast<uint32_t>(ks * 2), wide ? idesc_qk2 : idesc_qk,
+                       ks > 0 ? 1u : 0u);
+          for (int jj = j; jj <= last; ++jj) tc_commit(bar_k_empty((kc + jj) % L::KST));
+          if (last == w.n_kv - 1) tc_commit(bar_q_empty(qs));
+          for (int jj = j; jj <= last; ++jj) tc_commit(bar_s_full(jj));
         }
         __syncwarp();
+        j = last + 1;
       }
-      // O += P_j V_j, tiles in descending order as pass C releases them
+      // O += P_j V_j, tiles in descending order as pass C releases them. The
+      // V tiles and O's columns are waited for first (while the softmax is
+      // still in passes A / B), so each P@V step only waits for its P.
+      for (int i = 0; i < w.n_kv && ok; ++i) {
+        const int vg = vc + i;
+        ok = wait_all(bar_v_full(vg % L::VST), (vg / L::VST) & 1);
+      }
+      if (ok && !o_free) {
+        ok = wait_all(bar_o_empty, (k - 1) & 1);
+        o_free = true;
+      }
       for (int i = 0; i < w.n_kv && ok; ++i) {
         const int j = w.n_kv - 1 - i;
-        const int vg = vc + i;
-        const int s = vg % L::VST;
+        const int s = (vc + i) % L::VST;
         ok = wait_all(bar_p_full(j), (tile_par >> j) & 1u);
-        if (ok) ok = wait_all(bar_v_full(s), (vg / L::VST) & 1);
-        if (ok && !o_free) {
-          ok = wait_all(bar_o_empty, (k - 1) & 1);
-          o_free = true;
-        }
         if (!ok) break;
         tc_fence_after();
         if (leader) {
@@ -344,10 +359,11 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
   } else {
     // -------------------------------------------------------------- softmax
     constexpr int NE = 32;  // values per thread and key tile: 2 rows x 16 keys
-    const int quad = warp & 3;
-    const int blk = (warp >> 2) & 1;
-    const int half = warp >> 3;           // key columns [64 half, 64 half + 64) of each tile
-    const int pair = warp & 7;            // warps w and w + 8 hold the same rows
+    const int sw = warp;
+    const int quad = sw & 3;              // the TMEM lane quadrant this warp may access
+    const int blk = (sw >> 2) & 1;
+    const int half = sw >> 3;             // key columns [64 half, 64 half + 64) of each tile
+    const int pair = sw & 7;              // softmax warps sw and sw + 8 hold the same rows
     const int rb = quad * 32 + blk * 16;  // first row of this warp's block
     const int ra = rb + (lane >> 2);      // this thread's rows: ra and ra + 8
     const int cq = 2 * (lane & 3);
@@ -365,10 +381,12 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
     bool ok = true;
     uint32_t tile_par = 0;
 
-    // Raw Q K^T of this thread's columns of key tile j; keys outside the
-    // sequence, padding keys and (causal) keys after the row become -inf.
-    auto load_tile = [&](const Item& w, int j, uint32_t (&raw)[NE]) {
-      tmem_ld16x256b<8>(tmem + lane_off + j * BN + c0, raw);
+    auto issue_tile = [&](int j, uint32_t (&r)[NE]) {
+      tmem_ld16x256b<8>(tmem + lane_off + j * BN + c0, r);
+    };
+    // Completes issue_tile(j) for raw Q K^T: keys outside the sequence,
+    // padding keys and (causal) keys after the row become -inf.
+    auto finish_scores = [&](const Item& w, int j, uint32_t (&raw)[NE]) {
       const int n0 = j * BN + c0;
       uint32_t kbits[2];
       if constexpr (HAS_MASK) {
@@ -417,19 +435,32 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
     for (int it = blockIdx.x, k = 0; it < total_items && ok; it += gridDim.x, ++k) {
       const Item w = item_at(it);
 
-      // pass A: row maxima of the raw scores
+      // pass A: row maxima of the raw scores. TMEM reads run one key tile
+      // ahead (the next tile's load is issued before this tile's arithmetic;
+      // tcgen05.wait::ld waits for all of a thread's loads, so at most one
+      // tile is in flight when a wait is reached).
+      uint32_t buf[2][NE];
       float mraw[2][2] = {{-INFINITY, -INFINITY}, {-INFINITY, -INFINITY}};
-      for (int j = 0; j < w.n_kv && ok; ++j) {
-        ok = __all_sync(0xFFFFFFFFu, wait(bar_s_full(j), (tile_par >> j) & 1u));
-        if (!ok) break;
-        tc_fence_after();
-        uint32_t raw[NE];
-        load_tile(w, j, raw);
+      ok = __all_sync(0xFFFFFFFFu, wait(bar_s_full(0), tile_par & 1u));
+      if (!ok) break;
+      tc_fence_after();
+      issue_tile(0, buf[0]);
+#pragma unroll
+      for (int j = 0; j < L::kTiles; ++j) {
+        if (j >= w.n_kv) break;
+        finish_scores(w, j, buf[j & 1]);
+        if (j + 1 < w.n_kv) {
+          ok = __all_sync(0xFFFFFFFFu, wait(bar_s_full(j + 1), (tile_par >> (j + 1)) & 1u));
+          if (!ok) break;
+          tc_fence_after();
+          issue_tile(j + 1, buf[(j + 1) & 1]);
+        }
 #pragma unroll
         for (int e = 0; e < NE; e += 2) {
           const int h = (e >> 1) & 1;
           const int q = (e >> 2) & 1;
-          mraw[h][q] = fmaxf(mraw[h][q], fmaxf(__uint_as_float(raw[e]), __uint_as_float(raw[e + 1])));
+          mraw[h][q] = fmaxf(mraw[h][q], fmaxf(__uint_as_float(buf[j & 1][e]),
+                                               __uint_as_float(buf[j & 1][e + 1])));
         }
       }
       if (!ok) break;
@@ -457,10 +488,13 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
       }
 
       // pass B: e = exp(s - max) over the scores, written back in place
+      // (MUFU-bound: its loads are not pipelined, which would spill at the
+      // 96 registers a thread has with 18 warps)
       float part[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
       for (int j = 0; j < w.n_kv; ++j) {
-        uint32_t raw[NE];
-        load_tile(w, j, raw);
+        uint32_t (&raw)[NE] = buf[0];
+        issue_tile(j, raw);
+        finish_scores(w, j, raw);
 #pragma unroll
         for (int i = 0; i < NE / 2; ++i) {
           const int h = i & 1;
@@ -506,11 +540,14 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
       // in place in the registers and stored into the first 32 columns of
       // this half (16x128b shape: column 4g + i % 4 of repetition g holds
       // the key pair 8g + 2(i % 4), + 1 a thread holds)
-      for (int i = 0; i < w.n_kv; ++i) {
+      issue_tile(w.n_kv - 1, buf[0]);
+#pragma unroll
+      for (int i = 0; i < L::kTiles; ++i) {
+        if (i >= w.n_kv) break;
         const int j = w.n_kv - 1 - i;
-        uint32_t ev[NE];
-        tmem_ld16x256b<8>(tmem + lane_off + j * BN + c0, ev);
+        uint32_t (&ev)[NE] = buf[i & 1];
         tc_wait_ld_regs(ev);
+        if (j > 0) issue_tile(j - 1, buf[(i + 1) & 1]);
 #pragma unroll
         for (int q = 0; q < NE / 2; ++q) {
           const int h = q & 1;
