@@ -182,3 +182,33 @@ def test_layer_norm_equals_torch_bit_for_bit(dtype, width):
         res, norm = fused_residual_layer_norm(x, u, w, b, 1e-5)
         assert torch.equal(res, x + u)
         assert torch.equal(norm, F.layer_norm(x + u, (width,), w, b, 1e-5))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_many_row_pairs_per_warp_bit_for_bit(dtype):
+    # 16-bit rows of at most 1024 elements (a multiple of 8) take the staged
+    # form: persistent warps walk row pairs with the next pair's rows copied
+    # into shared memory ahead. 40001 rows give every warp several pairs (both
+    # stages turn over) and an odd last row; a ragged mask with both zeroing
+    # flags, the plain LayerNorm and the fused form all equal torch's ops.
+    g = torch.Generator(device="cuda").manual_seed(40001)
+    rows, width = 40001, 768
+    x = torch.randn(rows, width, device="cuda", generator=g).to(dtype)
+    u = torch.randn(rows, width, device="cuda", generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(width, device="cuda", generator=g)).to(dtype)
+    b = (0.1 * torch.randn(width, device="cuda", generator=g)).to(dtype)
+    mask = torch.rand(rows, device="cuda", generator=g) > 0.2
+    with torch.inference_mode():
+        assert torch.equal(layer_norm(x, w, b, 1e-5), F.layer_norm(x, (width,), w, b, 1e-5))
+        res, norm = fused_residual_layer_norm(x, u, w, b, 1e-5)
+        assert torch.equal(res, x + u)
+        assert torch.equal(norm, F.layer_norm(x + u, (width,), w, b, 1e-5))
+        res, norm = fused_residual_layer_norm(x, u, w, b, 1e-5, mask,
+                                              zero_invalid_residual=True,
+                                              zero_invalid_normalized=True)
+        keep = mask[:, None]
+        expect_res = torch.where(keep, x + u, torch.zeros_like(x))
+        assert torch.equal(res, expect_res)
+        expect_norm = torch.where(keep, F.layer_norm(expect_res, (width,), w, b, 1e-5),
+                                  torch.zeros_like(x))
+        assert torch.equal(norm, expect_norm)

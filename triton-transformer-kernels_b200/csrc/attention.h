@@ -76,6 +76,7 @@ struct RlnArgs {
   int dtype;
   float eps;
   uint32_t flags;
+  unsigned int* status;  // device status word (bounded waits of the staged path)
 };
 cudaError_t launch_residual_layer_norm(const RlnArgs& args, cudaStream_t stream);
 

@@ -376,6 +376,8 @@ int b200tk_residual_layer_norm_fwd(const void* x, const void* update, const void
   a.dtype = dtype;
   a.eps = eps;
   a.flags = flags;
+  int rc = status_address(&a.status);
+  if (rc != B200TK_OK) return rc;
   cudaError_t err = launch_residual_layer_norm(a, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "residual layer norm launch");
   return B200TK_OK;

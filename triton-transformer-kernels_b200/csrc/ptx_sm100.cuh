@@ -129,6 +129,18 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* desc, uint
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` from global memory into this CTA's shared
+// memory, completing that many transaction bytes on the mbarrier (no
+// multicast). Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // ---------------------------------------------------- CTA pairs (clusters)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
