@@ -16,6 +16,12 @@ this directory:
 
 16-bit tensors are stored as their raw uint16 bit patterns.
 Usage: python tests/golden/make_golden.py --reference <reference checkout>
+       [--check]
+
+--check writes nothing: it runs the reference and the oracle (oracle/) on the
+stored inputs on this host and requires their outputs to be bit-identical
+(the golden files themselves may differ from both by the host's CPU GEMM
+rounding when they were made on another instruction set).
 """
 
 from __future__ import annotations
@@ -98,11 +104,45 @@ def load_reference(root: Path):
     return organizer, _reference_attention
 
 
+def check(organizer, ref_attention) -> int:
+    """Reference vs oracle, bit for bit, on the stored inputs (same host)."""
+    sys.path.insert(0, str(HERE.parent.parent))
+    sys.path.insert(0, str(HERE.parent))
+    from oracle import explicit as oracle
+    import _golden
+
+    bad = 0
+    for case in _golden.attention_cases():
+        with torch.inference_mode():
+            args = (case["q"], case["k"], case["v"], case["mask"], case["causal"], None)
+            same = torch.equal(ref_attention(*args), oracle.reference_attention(*args))
+        bad += not same
+        print(f"attention {case['key']}: {'identical' if same else 'DIFFERENT'}")
+    data = _golden.load("model.npz")
+    for i, (b, s, dm, h, f, layers, causal, pad, seed) in enumerate(MODEL_CASES):
+        outs = []
+        for mod in (organizer, oracle):
+            torch.manual_seed(seed)
+            model = mod.BaselineTransformer(mod.TransformerConfig(b, s, dm, h, f, layers, causal)).eval()
+            x = torch.from_numpy(data[f"m{i}_x"])
+            mask = torch.from_numpy(data[f"m{i}_mask"]) if pad > 0 else None
+            with torch.inference_mode():
+                outs.append(model(x, mask))
+        same = torch.equal(outs[0], outs[1])
+        bad += not same
+        print(f"model m{i}: {'identical' if same else 'DIFFERENT'}")
+    print("all identical" if not bad else f"{bad} cases differ")
+    return 1 if bad else 0
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--reference", type=Path, required=True)
+    parser.add_argument("--check", action="store_true")
     args = parser.parse_args()
     organizer, ref_attention = load_reference(args.reference.resolve())
+    if args.check:
+        return check(organizer, ref_attention)
 
     out = {}
     for i, (b, s, h, d, dt, causal, mode, scale_in) in enumerate(ATTENTION_CASES):

@@ -1,6 +1,10 @@
 """Pin the oracle to the reference: its outputs must reproduce the golden
 vectors that tests/golden/make_golden.py produced by running the reference
-project's own code (CPU, no GPU needed)."""
+project's own code (CPU, no GPU needed). Outputs that pass through a CPU GEMM
+are held to a two-ulp bound of their scale (the BLAS rounds differently on
+other instruction sets); the rest are compared bit for bit. Bitwise identity
+of oracle and reference on one host is what ``make_golden.py --check``
+verifies."""
 
 from __future__ import annotations
 
@@ -20,8 +24,7 @@ def test_oracle_attention_matches_reference(case):
         out = oracle.reference_attention(
             case["q"], case["k"], case["v"], case["mask"], case["causal"], None
         )
-    assert out.dtype == case["out"].dtype
-    assert torch.equal(out, case["out"]), "oracle attention differs from the reference"
+    _golden.assert_close_to_golden(out, case["out"], f"attention {case['key']}")
 
 
 @pytest.mark.parametrize("case", _golden.attention_cases()[:6], ids=lambda c: c["key"])
@@ -70,7 +73,7 @@ def test_oracle_model_matches_reference(index):
         assert mask is None
     with torch.inference_mode():
         y = model(x, mask)
-    assert torch.equal(y, torch.from_numpy(data[f"m{index}_y"]))
+    _golden.assert_close_to_golden(y, torch.from_numpy(data[f"m{index}_y"]), f"model {index}")
 
 
 def test_oracle_compare_outputs_matches_reference():
