@@ -186,11 +186,9 @@ def test_layer_norm_equals_torch_bit_for_bit(dtype, width):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_many_row_pairs_per_warp_bit_for_bit(dtype):
-    # 16-bit rows of at most 1024 elements (a multiple of 8) take the staged
-    # form: persistent warps walk row pairs with the next pair's rows copied
-    # into shared memory ahead. 40001 rows give every warp several pairs (both
-    # stages turn over) and an odd last row; a ragged mask with both zeroing
-    # flags, the plain LayerNorm and the fused form all equal torch's ops.
+    # Many CTAs of row pairs (40001 rows: an odd last row), a ragged mask with
+    # both zeroing flags, the plain LayerNorm and the fused form: all equal
+    # torch's ops bit for bit.
     g = torch.Generator(device="cuda").manual_seed(40001)
     rows, width = 40001, 768
     x = torch.randn(rows, width, device="cuda", generator=g).to(dtype)

@@ -360,6 +360,34 @@ struct Quad {  // 4 consecutive elements: 16 bytes (fp32) or 8 bytes (16-bit)
     }
     return v;
   }
+  // x + u rounded to T, packed. 16-bit types add in pairs in their own type
+  // (add.rn.{bf16,f16}x2: the exact sum rounded once). That equals the fp32
+  // sum rounded to T: the fp32 sum of two 16-bit values is exact unless their
+  // exponents differ by more than 15 (bf16) / 12 (fp16), and then the smaller
+  // one is below half a unit of the larger one's 16-bit last place, so both
+  // roundings return the larger one.
+  __device__ __forceinline__ static Raw add_round(const Raw& x, const Raw& u) {
+    if constexpr (std::is_same_v<T, float>) {
+      Raw v;
+      v.x = __float_as_uint(__uint_as_float(x.x) + __uint_as_float(u.x));
+      v.y = __float_as_uint(__uint_as_float(x.y) + __uint_as_float(u.y));
+      v.z = __float_as_uint(__uint_as_float(x.z) + __uint_as_float(u.z));
+      v.w = __float_as_uint(__uint_as_float(x.w) + __uint_as_float(u.w));
+      return v;
+    } else {
+      using T2 = std::conditional_t<std::is_same_v<T, __half>, __half2, __nv_bfloat162>;
+      const uint32_t xw[2] = {x.x, x.y}, uw[2] = {u.x, u.y};
+      uint32_t w[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const T2 sum = __hadd2(*reinterpret_cast<const T2*>(&xw[i]), *reinterpret_cast<const T2*>(&uw[i]));
+        w[i] = *reinterpret_cast<const uint32_t*>(&sum);
+      }
+      Raw v;
+      v.x = w[0], v.y = w[1];
+      return v;
+    }
+  }
 };
 
 // ATen's kernel uses 128 threads per row; here one warp computes TWO rows,
@@ -376,44 +404,24 @@ struct Quad {  // 4 consecutive elements: 16 bytes (fp32) or 8 bytes (16-bit)
 // spread over the lanes (2 + 1 + 1 + 1 + 1 + 2 combinations per lane). The
 // element counts depend only on the width and the lane, so the reciprocal of
 // each node's count is shared by the two rows. 8 warps (16 rows) per CTA; no
-// shared memory and no block barrier. Rows of at most 1024 elements stay in
-// registers between the passes; longer ones are re-read (L2-resident).
+// shared memory and no block barrier. Each step's loads (one 4-element group
+// of every virtual thread of both rows) are issued before the previous step
+// is folded. Rows of at most 1024 elements stay in registers between the
+// passes; longer ones are re-read (L2-resident), again one step ahead.
 constexpr int kAtenThreads = 128;  // ATen's threads per row (4 warps)
 constexpr int kWelfordWarpsPerCta = 8;
 
-// Two fp32 values per instruction (sm_100 f32x2): each half is rounded exactly
-// as the scalar operation.
-__device__ __forceinline__ float2 add_x2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
-      "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
+// Two fp32 values per instruction (sm_100 f32x2, the compiler's paired
+// intrinsics): each half is rounded exactly as the scalar operation. a - b is
+// computed as fma(-1, b, a): -1 * b is exact, so the one rounding is that of
+// a - b (signed zeros included: an exact zero difference is +0 either way).
+__device__ __forceinline__ float2 add_x2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 sub_x2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
-      "sub.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
+  return __ffma2_rn(make_float2(-1.f, -1.f), b, a);
 }
-__device__ __forceinline__ float2 mul_x2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
-      "mul.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
+__device__ __forceinline__ float2 mul_x2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 fma_x2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
-      "mov.b64 z, {%6, %7};\n\tfma.rn.f32x2 x, x, y, z;\n\tmov.b64 {%0, %1}, x;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
+  return __ffma2_rn(a, b, c);
 }
 __device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
 
@@ -494,10 +502,10 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
   const int lane = threadIdx.x & 31;
   const int64_t row0 = 2 * (static_cast<int64_t>(blockIdx.x) * kWelfordWarpsPerCta + (threadIdx.x >> 5));
   if (row0 >= a.rows) return;  // whole warps leave together
+  const int n_quads = static_cast<int>(a.width / 4);
   // the second row; a last odd row is computed twice and stored once
   const bool two = row0 + 1 < a.rows;
   const int64_t rows[2] = {row0, two ? row0 + 1 : row0};
-  const int n_quads = static_cast<int>(a.width / 4);
   const bool has_update = !(a.flags & B200TK_RLN_NO_UPDATE);
   bool zero_res[2], zero_norm[2];
 #pragma unroll
@@ -523,20 +531,26 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
   PairState st[4];
 #pragma unroll
   for (int w = 0; w < 4; ++w) st[w] = PairState{splat(0.f), splat(0.f), 0.f};
-#pragma unroll
-  for (int k = 0; k < QPV; ++k) {
-    // this step's group of every virtual thread of both rows, loaded first
-    Raw xv[2][4], uv[2][4];
+  // each step's groups of every virtual thread of both rows; the next step's
+  // loads are in flight while this step is folded
+  Raw xv[2][2][4], uv[2][2][4];  // [buffer][row][virtual thread]
+  auto load_step = [&](int k, int buf) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const int qi = lane + 32 * w + kAtenThreads * k;
       const bool in = qi < n_quads;
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        xv[i][w] = in ? xq[i][qi] : Raw{};
-        uv[i][w] = (in && has_update) ? uq[i][qi] : Raw{};
+        xv[buf][i][w] = in ? xq[i][qi] : Raw{};
+        uv[buf][i][w] = (in && has_update) ? uq[i][qi] : Raw{};
       }
     }
+  };
+  load_step(0, 0);
+#pragma unroll
+  for (int k = 0; k < QPV; ++k) {
+    const int buf = k & 1;
+    if (k + 1 < QPV) load_step(k + 1, buf ^ 1);
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const int qi = lane + 32 * w + kAtenThreads * k;
@@ -544,26 +558,15 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
       float r[2][4];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        Q::unpack(xv[i][w], r[i]);
+        Raw packed;  // the rounded residual (or x itself), packed
         if (has_update) {
-          float fu[4];
-          Q::unpack(uv[i][w], fu);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float v = r[i][e] + fu[e];
-            if constexpr (!std::is_same_v<T, float>) v = round_t<T>(v);
-            r[i][e] = v;
-          }
-          if (zero_res[i]) r[i][0] = r[i][1] = r[i][2] = r[i][3] = 0.f;
-          if (i == 0 || two) rq[i][qi] = Q::pack(r[i]);
-        } else if (zero_res[i]) {
-          r[i][0] = r[i][1] = r[i][2] = r[i][3] = 0.f;
+          packed = zero_res[i] ? Raw{} : Q::add_round(xv[buf][i][w], uv[buf][i][w]);
+          if (i == 0 || two) rq[i][qi] = packed;
+        } else {
+          packed = zero_res[i] ? Raw{} : xv[buf][i][w];
         }
-      }
-      if constexpr (kHold) {
-        // r is a T value (rounded residual, or x itself): packing is exact
-        held[k * 4 + w][0] = Q::pack(r[0]);
-        held[k * 4 + w][1] = Q::pack(r[1]);
+        Q::unpack(packed, r[i]);
+        if constexpr (kHold) held[k * 4 + w][i] = packed;
       }
       // fold: the count before element e of group k is 4k + e, so
       // 1 / (4k + e + 1) folds to a correctly rounded constant
@@ -602,34 +605,53 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
   // itself for a plain LayerNorm) unless the rows are held in registers
   const Raw* src[2] = {has_update ? static_cast<const Raw*>(rq[0]) : xq[0],
                        has_update ? static_cast<const Raw*>(rq[1]) : xq[1]};
+  // rows that are not held: each step's groups (and weight / bias groups)
+  // are re-read, the next step's while this one is normalised
+  Raw sv[kHold ? 1 : 2][2][4], wsv[kHold ? 1 : 2][4], bsv[kHold ? 1 : 2][4];
+  auto reload_step = [&](int k, int buf) {
+    if constexpr (!kHold) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const int qi = lane + 32 * w + kAtenThreads * k;
+        const bool in = qi < n_quads;
+        sv[buf][0][w] = (in && !zero_res[0]) ? src[0][qi] : Raw{};
+        sv[buf][1][w] = (in && !zero_res[1]) ? src[1][qi] : Raw{};
+        if constexpr (!kPrefetch) {
+          wsv[buf][w] = in ? wq[qi] : Raw{};
+          bsv[buf][w] = (in && bq != nullptr) ? bq[qi] : Raw{};
+        }
+      }
+    }
+  };
+  reload_step(0, 0);
 #pragma unroll
   for (int k = 0; k < QPV; ++k) {
+    const int buf = kHold ? 0 : (k & 1);
+    if (k + 1 < QPV) reload_step(k + 1, buf ^ 1);
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const int qi = lane + 32 * w + kAtenThreads * k;
       if (qi >= n_quads) continue;
       float2 r[4];
       float fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f};
-      if constexpr (kHold) {
+      {
         float r0[4], r1[4];
-        Q::unpack(held[k * 4 + w][0], r0);
-        Q::unpack(held[k * 4 + w][1], r1);
+        if constexpr (kHold) {
+          Q::unpack(held[k * 4 + w][0], r0);
+          Q::unpack(held[k * 4 + w][1], r1);
+        } else {
+          Q::unpack(sv[buf][0][w], r0);
+          Q::unpack(sv[buf][1][w], r1);
+        }
 #pragma unroll
         for (int e = 0; e < 4; ++e) r[e] = make_float2(r0[e], r1[e]);
-      } else {
-        float r0[4], r1[4];
-        Q::unpack(src[0][qi], r0);
-        Q::unpack(src[1][qi], r1);
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          r[e] = make_float2(zero_res[0] ? 0.f : r0[e], zero_res[1] ? 0.f : r1[e]);
       }
       if constexpr (kPrefetch) {
         Q::unpack(wv[k * 4 + w], fw);
         if (bq != nullptr) Q::unpack(bv[k * 4 + w], fb);
       } else {
-        Q::unpack(wq[qi], fw);
-        if (bq != nullptr) Q::unpack(bq[qi], fb);
+        Q::unpack(wsv[buf][w], fw);
+        if (bq != nullptr) Q::unpack(bsv[buf][w], fb);
       }
       float o[2][4];
 #pragma unroll
@@ -647,245 +669,6 @@ __global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(c
       if (two) nq[1][qi] = Q::pack(o[1]);
     }
   }
-}
-
-// Staged variant of rln_welford_kernel for 16-bit rows of at most 1024
-// elements (width a multiple of 8, 16-byte aligned rows): persistent warps
-// walk row pairs, and while a warp computes one pair the next pair's x and
-// update rows are already in flight into its other shared-memory stage (bulk
-// async copies completing on that stage's mbarrier). Every warp so keeps a
-// pair's bytes in flight through its arithmetic; the register version holds
-// 16 warps per SM at 112 registers, each stalled on its own loads (measured
-// 0.59 of HBM bandwidth at C5's shape). The arithmetic is rln_welford_kernel's
-// in the same order (outputs bit-identical); the rounded residual is written
-// back over the staged x row for the second pass, and weight / bias stay in
-// registers for the whole launch. Waits are bounded: a copy that does not
-// land within the limit sets the status bit, and the warp waits (bounded)
-// for its copies still in flight and stops.
-constexpr int kStagedWarps = 4;
-constexpr int kStagedMaxWidth = 4 * kAtenThreads * 2;  // QPV <= 2
-
-template <typename T, int QPV>
-__global__ void __launch_bounds__(32 * kStagedWarps, 4) rln_staged_kernel(const RlnArgs a) {
-  using Q = Quad<T>;
-  using Raw = typename Q::Raw;
-  static_assert(!std::is_same_v<T, float> && QPV <= 2, "16-bit rows of at most 1024 elements");
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int lane = threadIdx.x & 31;
-  const int wid = threadIdx.x >> 5;
-  const int n_quads = static_cast<int>(a.width / 4);
-  const bool has_update = !(a.flags & B200TK_RLN_NO_UPDATE);
-  const uint32_t row_bytes = static_cast<uint32_t>(a.width) * sizeof(T);
-  const uint32_t stage_bytes = 4 * row_bytes;  // x row 0, x row 1, update row 0, update row 1
-  uint8_t* wbuf = smem + 128 + static_cast<size_t>(wid) * 2 * stage_bytes;
-  const uint32_t bar0 = smem_u32(smem) + 16 * wid;  // this warp's two stage barriers
-  if (lane == 0) {
-    mbar_init(bar0, 1);
-    mbar_init(bar0 + 8, 1);
-    fence_mbarrier_init();
-  }
-  __syncwarp();
-
-  const int64_t pairs = (a.rows + 1) / 2;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kStagedWarps;
-  const T* xg = static_cast<const T*>(a.x);
-  const T* ug = static_cast<const T*>(a.update);
-  int issued[2] = {0, 0};
-  auto issue = [&](int64_t pair, int stage) {  // lane 0
-    const int64_t r0 = 2 * pair, r1 = r0 + 1 < a.rows ? r0 + 1 : r0;
-    const uint32_t bar = bar0 + 8 * stage;
-    const uint32_t dst = smem_u32(wbuf + stage * stage_bytes);
-    mbar_arrive_expect_tx(bar, (has_update ? 4 : 2) * row_bytes);
-    bulk_load(dst, xg + r0 * a.width, row_bytes, bar);
-    bulk_load(dst + row_bytes, xg + r1 * a.width, row_bytes, bar);
-    if (has_update) {
-      bulk_load(dst + 2 * row_bytes, ug + r0 * a.width, row_bytes, bar);
-      bulk_load(dst + 3 * row_bytes, ug + r1 * a.width, row_bytes, bar);
-    }
-    ++issued[stage];
-  };
-  int64_t pair = static_cast<int64_t>(blockIdx.x) * kStagedWarps + wid;
-  if (pair < pairs && lane == 0) issue(pair, 0);
-
-  // weight / bias groups of this lane, for every pair of the launch
-  const Raw* wq = static_cast<const Raw*>(a.weight);
-  const Raw* bq = static_cast<const Raw*>(a.bias);
-  Raw wv[QPV * 4], bv[QPV * 4];
-#pragma unroll
-  for (int g = 0; g < QPV * 4; ++g) {
-    const int qi = lane + 32 * (g & 3) + kAtenThreads * (g >> 2);
-    wv[g] = qi < n_quads ? wq[qi] : Raw{};
-    bv[g] = (qi < n_quads && bq != nullptr) ? bq[qi] : Raw{};
-  }
-  const float width = static_cast<float>(a.width);
-
-  bool ok = true;
-  for (int it = 0; pair < pairs; pair += stride, ++it) {
-    const int stage = it & 1;
-    if (pair + stride < pairs) {
-      // every lane's reads and writes of the other stage (previous pair) are
-      // ordered before the copies that overwrite it
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) issue(pair + stride, stage ^ 1);
-    }
-    int got = 1;
-    if (lane == 0) {
-      const uint32_t bar = bar0 + 8 * stage;
-      const uint32_t par = (it >> 1) & 1;
-      got = mbar_try_wait(bar, par) ? 1 : 0;
-      if (!got) {
-        const uint64_t t0 = globaltimer_ns();
-        while (!(got = mbar_try_wait(bar, par) ? 1 : 0) && globaltimer_ns() - t0 < 2000000000ull) {
-        }
-        if (!got) atomicOr(a.status, B200TK_STATUS_PIPELINE_TIMEOUT);
-      }
-    }
-    __syncwarp();
-    if (!__shfl_sync(0xFFFFFFFFu, got, 0)) {
-      ok = false;
-      break;
-    }
-    Raw* sx[2] = {reinterpret_cast<Raw*>(wbuf + stage * stage_bytes),
-                  reinterpret_cast<Raw*>(wbuf + stage * stage_bytes + row_bytes)};
-    const Raw* su[2] = {reinterpret_cast<const Raw*>(wbuf + stage * stage_bytes + 2 * row_bytes),
-                        reinterpret_cast<const Raw*>(wbuf + stage * stage_bytes + 3 * row_bytes)};
-    const int64_t row0 = 2 * pair;
-    const bool two = row0 + 1 < a.rows;
-    const int64_t rows[2] = {row0, two ? row0 + 1 : row0};
-    bool zero_res[2], zero_norm[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const bool valid = a.mask == nullptr || a.mask[rows[i]] != 0;
-      zero_res[i] = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_RESIDUAL);
-      zero_norm[i] = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_NORMALIZED);
-    }
-    Raw* rq[2];
-    Raw* nq[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      rq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.residual_out) + rows[i] * a.width);
-      nq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + rows[i] * a.width);
-    }
-
-    // pass 1: rounded residual (stored, and written back over the staged x
-    // row) and the Welford states of the four virtual threads, both rows
-    PairState st[4];
-#pragma unroll
-    for (int w = 0; w < 4; ++w) st[w] = PairState{splat(0.f), splat(0.f), 0.f};
-#pragma unroll
-    for (int k = 0; k < QPV; ++k) {
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const int qi = lane + 32 * w + kAtenThreads * k;
-        if (qi >= n_quads) continue;
-        float r[2][4];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          Q::unpack(sx[i][qi], r[i]);
-          if (has_update) {
-            float fu[4];
-            Q::unpack(su[i][qi], fu);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) r[i][e] = round_t<T>(r[i][e] + fu[e]);
-            if (zero_res[i]) r[i][0] = r[i][1] = r[i][2] = r[i][3] = 0.f;
-            const Raw packed = Q::pack(r[i]);
-            if (i == 0 || two) rq[i][qi] = packed;
-            sx[i][qi] = packed;
-          } else if (zero_res[i]) {
-            r[i][0] = r[i][1] = r[i][2] = r[i][3] = 0.f;
-            sx[i][qi] = Q::pack(r[i]);
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 v = make_float2(r[0][e], r[1][e]);
-          const float2 delta = sub_x2(v, st[w].mean);
-          st[w].mean = fma_x2(delta, splat(1.f / static_cast<float>(4 * k + e + 1)), st[w].mean);
-          st[w].m2 = fma_x2(delta, sub_x2(v, st[w].mean), st[w].m2);
-        }
-        st[w].count = static_cast<float>(4 * (k + 1));
-      }
-    }
-    const PairState root = pair_tree(st, lane);
-    const float2 mean = make_float2(__shfl_sync(0xFFFFFFFFu, root.mean.x, 0),
-                                    __shfl_sync(0xFFFFFFFFu, root.mean.y, 0));
-    const float2 m2 = make_float2(__shfl_sync(0xFFFFFFFFu, root.m2.x, 0),
-                                  __shfl_sync(0xFFFFFFFFu, root.m2.y, 0));
-    const float2 rstd = make_float2(rsqrtf(__fadd_rn(__fdiv_rn(m2.x, width), a.eps)),
-                                    rsqrtf(__fadd_rn(__fdiv_rn(m2.y, width), a.eps)));
-
-    // pass 2: normalised rows from the staged rounded residual
-#pragma unroll
-    for (int k = 0; k < QPV; ++k) {
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const int qi = lane + 32 * w + kAtenThreads * k;
-        if (qi >= n_quads) continue;
-        float r0[4], r1[4], fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f};
-        Q::unpack(sx[0][qi], r0);
-        Q::unpack(sx[1][qi], r1);
-        Q::unpack(wv[k * 4 + w], fw);
-        if (bq != nullptr) Q::unpack(bv[k * 4 + w], fb);
-        float o[2][4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          // n = w * (rstd * (r - mean)) + b, both rows per instruction
-          const float2 c = mul_x2(rstd, sub_x2(make_float2(r0[e], r1[e]), mean));
-          const float2 n = bq != nullptr ? fma_x2(splat(fw[e]), c, splat(fb[e]))
-                                         : mul_x2(splat(fw[e]), c);
-          o[0][e] = n.x;
-          o[1][e] = n.y;
-        }
-        if (zero_norm[0]) o[0][0] = o[0][1] = o[0][2] = o[0][3] = 0.f;
-        if (zero_norm[1]) o[1][0] = o[1][1] = o[1][2] = o[1][3] = 0.f;
-        nq[0][qi] = Q::pack(o[0]);
-        if (two) nq[1][qi] = Q::pack(o[1]);
-      }
-    }
-    __syncwarp();
-  }
-  if (!ok && lane == 0) {
-    // drain: every copy this warp started lands before the CTA can exit
-    for (int sg = 0; sg < 2; ++sg) {
-      if (issued[sg] == 0) continue;
-      const uint32_t par = (issued[sg] - 1) & 1;
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(bar0 + 8 * sg, par) && globaltimer_ns() - t0 < 2000000000ull) {
-      }
-    }
-  }
-}
-
-int current_sm_count();
-
-template <typename T>
-cudaError_t launch_staged(const RlnArgs& a, cudaStream_t stream) {
-  const int qpv = static_cast<int>((a.width / 4 + kAtenThreads - 1) / kAtenThreads);
-  const int smem = 128 + kStagedWarps * 2 * 4 * static_cast<int>(a.width) * static_cast<int>(sizeof(T));
-  const int64_t pairs = (a.rows + 1) / 2;
-  const int sms = current_sm_count();
-  // CTAs resident per SM by shared memory (227 KB per SM usable)
-  const int per_sm = (227 * 1024) / smem > 0 ? (227 * 1024) / smem : 1;
-  int64_t grid = (pairs + kStagedWarps - 1) / kStagedWarps;
-  if (grid > static_cast<int64_t>(sms) * per_sm) grid = static_cast<int64_t>(sms) * per_sm;
-  auto kernel = qpv == 1 ? rln_staged_kernel<T, 1> : rln_staged_kernel<T, 2>;
-  static std::atomic<uint64_t> configured{0};
-  int device = 0;
-  cudaError_t err = cudaGetDevice(&device);
-  if (err != cudaSuccess) return err;
-  const uint64_t bit = device < 64 ? (uint64_t(1) << device) : 0;
-  if (bit == 0 || !(configured.load(std::memory_order_acquire) & bit)) {
-    err = cudaFuncSetAttribute(rln_staged_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               128 + kStagedWarps * 2 * 4 * kStagedMaxWidth * static_cast<int>(sizeof(T)));
-    if (err == cudaSuccess)
-      err = cudaFuncSetAttribute(rln_staged_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 128 + kStagedWarps * 2 * 4 * kStagedMaxWidth * static_cast<int>(sizeof(T)));
-    if (err != cudaSuccess) return err;
-    configured.fetch_or(bit, std::memory_order_acq_rel);
-  }
-  kernel<<<static_cast<unsigned>(grid), 32 * kStagedWarps, smem, stream>>>(a);
-  return cudaGetLastError();
 }
 
 template <typename T>
@@ -998,11 +781,6 @@ cudaError_t launch_typed(const RlnArgs& a, cudaStream_t stream) {
                           (a.bias == nullptr || aligned(a.bias)) &&
                           ((a.flags & B200TK_RLN_NO_UPDATE) ||
                            (aligned(a.update) && aligned(a.residual_out)));
-  if constexpr (!std::is_same_v<T, float>) {
-    // rows of at most 1024 elements, whole 16-byte copies: the staged form
-    if (welford_ok && a.width % 8 == 0 && a.width <= kStagedMaxWidth && a.status != nullptr)
-      return launch_staged<T>(a, stream);
-  }
   if (welford_ok) return launch_welford<T>(a, stream);
   const bool vec_ok = a.width % EPV == 0 && aligned(a.x) && aligned(a.weight) &&
                       aligned(a.normalized_out) && (a.bias == nullptr || aligned(a.bias)) &&
