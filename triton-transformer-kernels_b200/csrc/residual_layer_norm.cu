@@ -401,13 +401,13 @@ struct Quad {  // 4 consecutive elements: 16 bytes (fp32) or 8 bytes (16-bit)
 // levels N16[w][l] = C(leaf[w][l], leaf[w][l + 16]), N8 = C(N16[l],
 // N16[l + 8]), ..., N1[w]; then C(N1[0], N1[2]), C(N1[1], N1[3]) and their
 // combination, C(own, other) with "own" the lower index -- with its nodes
-// spread over the lanes (2 + 1 + 1 + 1 + 1 + 2 combinations per lane). The
-// element counts depend only on the width and the lane, so the reciprocal of
-// each node's count is shared by the two rows. 8 warps (16 rows) per CTA; no
-// shared memory and no block barrier. Each step's loads (one 4-element group
-// of every virtual thread of both rows) are issued before the previous step
-// is folded. Rows of at most 1024 elements stay in registers between the
-// passes; longer ones are re-read (L2-resident), again one step ahead.
+// spread over the lanes (2 + 1 + 1 + 1 + 1 + 2 combinations per lane), with
+// every node's coefficients computed once per CTA (they depend only on the
+// width and the lane). 8 warps (16 rows) per CTA. Each step's loads (one
+// 4-element group of every virtual thread of both rows) are issued before the
+// previous step is folded. Rows of at most 1024 elements stay in registers
+// between the passes; longer ones are re-read (L2-resident), again one step
+// ahead.
 constexpr int kAtenThreads = 128;  // ATen's threads per row (4 warps)
 constexpr int kWelfordWarpsPerCta = 8;
 
@@ -425,7 +425,121 @@ __device__ __forceinline__ float2 fma_x2(float2 a, float2 b, float2 c) {
 }
 __device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
 
-// Welford states of one virtual thread for the warp's two rows (count shared).
+// ATen's combination of two Welford states, C(own b, other a): n = n_a + n_b,
+// coef = 1 / n (correctly rounded), mean = (n_a coef) mean_a + (n_b coef)
+// mean_b (one fused multiply-add), m2 = ((delta^2) n_a)(n_b coef) + (m2_a +
+// m2_b) with delta = mean_b - mean_a; n = 0 gives an empty state. Every count
+// in the tree depends only on the width and the lane, so the coefficients of
+// a lane's eight combination sites (n_a coef, n_b coef, n_a) are found once
+// per CTA (tree_coefs) and the per-row tree (pair_tree_c) only moves and
+// combines means and m2. A site with n = 0 combines two empty states (mean
+// and m2 zero), which its zero coefficients reproduce.
+constexpr int kTreeSites = 8;
+struct PairMoments {  // mean and m2 of one virtual thread, both rows
+  float2 mean, m2;
+};
+struct SiteCoef {
+  float na, nb, ca;
+};
+
+__device__ __forceinline__ SiteCoef site_coef(float cb, float ca) {
+  const float count = __fadd_rn(ca, cb);
+  if (!(count > 0.f)) return {0.f, 0.f, 0.f};
+  const float coef = __frcp_rn(count);
+  return {__fmul_rn(ca, coef), __fmul_rn(cb, coef), ca};
+}
+
+__device__ __forceinline__ PairMoments combine_c(const PairMoments& b, const PairMoments& a,
+                                                 const SiteCoef& c) {
+  const float2 delta = sub_x2(b.mean, a.mean);
+  const float2 mean = fma_x2(splat(c.na), a.mean, mul_x2(splat(c.nb), b.mean));
+  const float2 m2 =
+      fma_x2(mul_x2(mul_x2(delta, delta), splat(c.ca)), splat(c.nb), add_x2(a.m2, b.m2));
+  return {mean, m2};
+}
+
+// The tree's sites in order: x, y (N16 of ATen warps 0, 2 / 1, 3), N8, N4,
+// N2, N1, C(N1[0], N1[2]) / C(N1[1], N1[3]), root; the counts move between
+// lanes as the states do in pair_tree_c.
+__device__ __forceinline__ void tree_coefs(const float (&leaf)[4], int lane,
+                                           SiteCoef (&site)[kTreeSites]) {
+  const bool lo = lane < 16;
+  const float ra = __shfl_xor_sync(0xFFFFFFFFu, lo ? leaf[1] : leaf[0], 16);
+  const float rb = __shfl_xor_sync(0xFFFFFFFFu, lo ? leaf[3] : leaf[2], 16);
+  site[0] = lo ? site_coef(leaf[0], ra) : site_coef(ra, leaf[1]);
+  site[1] = lo ? site_coef(leaf[2], rb) : site_coef(rb, leaf[3]);
+  const float x = __fadd_rn(lo ? ra : leaf[1], lo ? leaf[0] : ra);
+  const float y = __fadd_rn(lo ? rb : leaf[3], lo ? leaf[2] : rb);
+  const int w = lane >> 3, l = lane & 7;
+  const int s1 = l + 16 * (w & 1), s2 = s1 + 8;
+  const float x1 = __shfl_sync(0xFFFFFFFFu, x, s1), x2 = __shfl_sync(0xFFFFFFFFu, x, s2);
+  const float y1 = __shfl_sync(0xFFFFFFFFu, y, s1), y2 = __shfl_sync(0xFFFFFFFFu, y, s2);
+  site[2] = w < 2 ? site_coef(x1, x2) : site_coef(y1, y2);
+  float n = w < 2 ? __fadd_rn(x2, x1) : __fadd_rn(y2, y1);
+#pragma unroll
+  for (int k = 3, off = 4; off > 0; off >>= 1, ++k) {
+    const float o = __shfl_down_sync(0xFFFFFFFFu, n, off);
+    site[k] = site_coef(n, o);
+    n = __fadd_rn(o, n);
+  }
+  const float o16 = __shfl_down_sync(0xFFFFFFFFu, n, 16);
+  site[6] = site_coef(n, o16);
+  n = __fadd_rn(o16, n);
+  site[7] = site_coef(n, __shfl_down_sync(0xFFFFFFFFu, n, 8));
+}
+
+__device__ __forceinline__ PairMoments shfl_m(const PairMoments& v, int src) {
+  return {make_float2(__shfl_sync(0xFFFFFFFFu, v.mean.x, src),
+                      __shfl_sync(0xFFFFFFFFu, v.mean.y, src)),
+          make_float2(__shfl_sync(0xFFFFFFFFu, v.m2.x, src), __shfl_sync(0xFFFFFFFFu, v.m2.y, src))};
+}
+__device__ __forceinline__ PairMoments shfl_xor_m(const PairMoments& v, int mask) {
+  return {make_float2(__shfl_xor_sync(0xFFFFFFFFu, v.mean.x, mask),
+                      __shfl_xor_sync(0xFFFFFFFFu, v.mean.y, mask)),
+          make_float2(__shfl_xor_sync(0xFFFFFFFFu, v.m2.x, mask),
+                      __shfl_xor_sync(0xFFFFFFFFu, v.m2.y, mask))};
+}
+__device__ __forceinline__ PairMoments shfl_down_m(const PairMoments& v, int off) {
+  return {make_float2(__shfl_down_sync(0xFFFFFFFFu, v.mean.x, off),
+                      __shfl_down_sync(0xFFFFFFFFu, v.mean.y, off)),
+          make_float2(__shfl_down_sync(0xFFFFFFFFu, v.m2.x, off),
+                      __shfl_down_sync(0xFFFFFFFFu, v.m2.y, off))};
+}
+
+// The root of ATen's combination tree over the 128 virtual-thread states
+// leaf[w] (this lane's virtual threads 32w + lane), both rows, with the
+// sites' coefficients (coef(k): this lane's site k); valid in lane 0.
+// N16: lane j < 16 builds (w = 0, 2; l = j), lane j >= 16 (w = 1, 3;
+// l = j - 16), the partner lane j ^ 16 holding the other leaf of each pair.
+// N8[w][l] (l < 8) in lane 8w + l: N16[w][l] and N16[w][l + 8] sit in lanes
+// l + 16 (w & 1) and l + 8 + 16 (w & 1), in x for w < 2 and y for w >= 2.
+// N4, N2, N1 within each group of 8 lanes (lane 8w holds N1[w]); then
+// C(N1[0], N1[2]) in lane 0, C(N1[1], N1[3]) in lane 8, and their combination.
+template <typename Coef>
+__device__ __forceinline__ PairMoments pair_tree_c(const PairMoments (&leaf)[4], int lane,
+                                                   const Coef& coef) {
+  const bool lo = lane < 16;
+  const PairMoments ra = shfl_xor_m(lo ? leaf[1] : leaf[0], 16);
+  const PairMoments rb = shfl_xor_m(lo ? leaf[3] : leaf[2], 16);
+  const SiteCoef c0 = coef(0), c1 = coef(1);
+  const PairMoments x = lo ? combine_c(leaf[0], ra, c0) : combine_c(ra, leaf[1], c0);
+  const PairMoments y = lo ? combine_c(leaf[2], rb, c1) : combine_c(rb, leaf[3], c1);
+  const int w = lane >> 3, l = lane & 7;
+  const int s1 = l + 16 * (w & 1), s2 = s1 + 8;
+  const PairMoments x1 = shfl_m(x, s1), x2 = shfl_m(x, s2);
+  const PairMoments y1 = shfl_m(y, s1), y2 = shfl_m(y, s2);
+  const SiteCoef c2 = coef(2);
+  PairMoments n = w < 2 ? combine_c(x1, x2, c2) : combine_c(y1, y2, c2);
+#pragma unroll
+  for (int k = 3, off = 4; off > 0; off >>= 1, ++k) n = combine_c(n, shfl_down_m(n, off), coef(k));
+  n = combine_c(n, shfl_down_m(n, 16), coef(6));
+  return combine_c(n, shfl_down_m(n, 8), coef(7));
+}
+
+// Per-row form of the tree (CTAs of one pass over 16 rows, where one set of
+// coefficients per CTA would not pay for its barrier): Welford states of one
+// virtual thread for the warp's two rows, count shared, combined with the
+// counts carried along.
 struct PairState {
   float2 mean, m2;
   float count;
@@ -491,207 +605,283 @@ __device__ __forceinline__ PairState pair_tree(const PairState (&leaf)[4], int l
   return pair_combine(n, shfl_down_pair(n, 8));
 }
 
+// Rows held in registers (at most 1024 elements): persistent CTAs, each warp
+// walking row pairs with stride gridDim.x * 8; the tree coefficients and a
+// shared-memory copy of weight and bias are made once per CTA (C5's 768-wide
+// rows: 0.27 ms against 0.28-0.30 ms for CTAs of one pass over 16 rows).
+// Wider rows: CTAs of one pass over 16 rows with the per-row tree, whose load
+// latency the resident CTAs cover better and which need no block barrier
+// (C3's 4096-wide rows: 0.36 ms against 0.39-0.41 ms persistent).
 template <typename T, int QPV>  // QPV: 4-element groups per ATen thread (width <= 512 * QPV)
-__global__ void __launch_bounds__(32 * kWelfordWarpsPerCta) rln_welford_kernel(const RlnArgs a) {
+__global__ void __launch_bounds__(32 * kWelfordWarpsPerCta, 2) rln_welford_kernel(const RlnArgs a) {
   using Q = Quad<T>;
   using Raw = typename Q::Raw;
   constexpr bool kHold = QPV <= 2;  // keep the rows in registers between the passes
-  // 16-bit held rows also take their weight / bias groups early (fp32 rows
-  // would need twice the registers)
+  // 16-bit held rows read their weight / bias groups from a copy in shared
+  // memory made once per CTA
   constexpr bool kPrefetch = kHold && !std::is_same_v<T, float>;
+  constexpr bool kPersist = kHold;
   const int lane = threadIdx.x & 31;
-  const int64_t row0 = 2 * (static_cast<int64_t>(blockIdx.x) * kWelfordWarpsPerCta + (threadIdx.x >> 5));
-  if (row0 >= a.rows) return;  // whole warps leave together
   const int n_quads = static_cast<int>(a.width / 4);
-  // the second row; a last odd row is computed twice and stored once
-  const bool two = row0 + 1 < a.rows;
-  const int64_t rows[2] = {row0, two ? row0 + 1 : row0};
   const bool has_update = !(a.flags & B200TK_RLN_NO_UPDATE);
-  bool zero_res[2], zero_norm[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const bool valid = a.mask == nullptr || a.mask[rows[i]] != 0;
-    zero_res[i] = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_RESIDUAL);
-    zero_norm[i] = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_NORMALIZED);
-  }
   const bool tf32 = std::is_same_v<T, float> && (a.flags & B200TK_RLN_ROUND_TF32);
-  const Raw* xq[2];
-  const Raw* uq[2];
-  Raw* rq[2];
-  Raw* nq[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    xq[i] = reinterpret_cast<const Raw*>(static_cast<const T*>(a.x) + rows[i] * a.width);
-    uq[i] = reinterpret_cast<const Raw*>(static_cast<const T*>(a.update) + rows[i] * a.width);
-    rq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.residual_out) + rows[i] * a.width);
-    nq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + rows[i] * a.width);
-  }
+  const float width = static_cast<float>(a.width);
 
-  Raw held[kHold ? QPV * 4 : 1][2];  // the rounded residual groups of both rows, packed
-  PairState st[4];
-#pragma unroll
-  for (int w = 0; w < 4; ++w) st[w] = PairState{splat(0.f), splat(0.f), 0.f};
+  const int64_t pairs = (a.rows + 1) / 2;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWelfordWarpsPerCta;
+  int64_t pair = static_cast<int64_t>(blockIdx.x) * kWelfordWarpsPerCta + (threadIdx.x >> 5);
+  // rows of a pair; a last odd row is computed twice and stored once
+  auto row_of = [&](int64_t pr, int i) {
+    const int64_t r = 2 * pr + i;
+    return r < a.rows ? r : a.rows - 1;
+  };
   // each step's groups of every virtual thread of both rows; the next step's
   // loads are in flight while this step is folded
   Raw xv[2][2][4], uv[2][2][4];  // [buffer][row][virtual thread]
-  auto load_step = [&](int k, int buf) {
+  auto load_step = [&](int64_t pr, int k, int buf) {
+    const T* xr[2] = {static_cast<const T*>(a.x) + row_of(pr, 0) * a.width,
+                      static_cast<const T*>(a.x) + row_of(pr, 1) * a.width};
+    const T* ur[2] = {static_cast<const T*>(a.update) + row_of(pr, 0) * a.width,
+                      static_cast<const T*>(a.update) + row_of(pr, 1) * a.width};
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const int qi = lane + 32 * w + kAtenThreads * k;
       const bool in = qi < n_quads;
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        xv[buf][i][w] = in ? xq[i][qi] : Raw{};
-        uv[buf][i][w] = (in && has_update) ? uq[i][qi] : Raw{};
+        xv[buf][i][w] = in ? reinterpret_cast<const Raw*>(xr[i])[qi] : Raw{};
+        uv[buf][i][w] = (in && has_update) ? reinterpret_cast<const Raw*>(ur[i])[qi] : Raw{};
       }
     }
   };
-  load_step(0, 0);
+  // element count of this lane's virtual thread w
+  const auto leaf_count = [&](int w) {
+    int groups = 0;
 #pragma unroll
-  for (int k = 0; k < QPV; ++k) {
-    const int buf = k & 1;
-    if (k + 1 < QPV) load_step(k + 1, buf ^ 1);
+    for (int k = 0; k < QPV; ++k) groups += (lane + 32 * w + kAtenThreads * k < n_quads) ? 1 : 0;
+    return static_cast<float>(4 * groups);
+  };
+  __shared__ float s_coef[kPersist ? 3 : 1][kTreeSites][32];  // n_a / n, n_b / n, n_a
+  if (kPersist && threadIdx.x < 32) {
+    float leaf[4];
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const int qi = lane + 32 * w + kAtenThreads * k;
-      if (qi >= n_quads) continue;
-      float r[2][4];
+    for (int w = 0; w < 4; ++w) leaf[w] = leaf_count(w);
+    SiteCoef site[kTreeSites];
+    tree_coefs(leaf, lane, site);
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        Raw packed;  // the rounded residual (or x itself), packed
-        if (has_update) {
-          packed = zero_res[i] ? Raw{} : Q::add_round(xv[buf][i][w], uv[buf][i][w]);
-          if (i == 0 || two) rq[i][qi] = packed;
-        } else {
-          packed = zero_res[i] ? Raw{} : xv[buf][i][w];
-        }
-        Q::unpack(packed, r[i]);
-        if constexpr (kHold) held[k * 4 + w][i] = packed;
-      }
-      // fold: the count before element e of group k is 4k + e, so
-      // 1 / (4k + e + 1) folds to a correctly rounded constant
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 v = make_float2(r[0][e], r[1][e]);
-        const float2 delta = sub_x2(v, st[w].mean);
-        st[w].mean = fma_x2(delta, splat(1.f / static_cast<float>(4 * k + e + 1)), st[w].mean);
-        st[w].m2 = fma_x2(delta, sub_x2(v, st[w].mean), st[w].m2);
-      }
-      st[w].count = static_cast<float>(4 * (k + 1));
+    for (int k = 0; k < kTreeSites; ++k) {
+      s_coef[0][k][lane] = site[k].na;
+      s_coef[1][k][lane] = site[k].nb;
+      s_coef[2][k][lane] = site[k].ca;
     }
   }
-  // weight / bias groups of this lane, requested before the combination
-  // tree so that their (L2) latency overlaps it
   const Raw* wq = static_cast<const Raw*>(a.weight);
   const Raw* bq = static_cast<const Raw*>(a.bias);
-  Raw wv[kPrefetch ? QPV * 4 : 1], bv[kPrefetch ? QPV * 4 : 1];
+  __shared__ Raw s_w[kPrefetch ? QPV * kAtenThreads : 1], s_b[kPrefetch ? QPV * kAtenThreads : 1];
   if constexpr (kPrefetch) {
-#pragma unroll
-    for (int g = 0; g < QPV * 4; ++g) {
-      const int qi = lane + 32 * (g & 3) + kAtenThreads * (g >> 2);
-      wv[g] = qi < n_quads ? wq[qi] : Raw{};
-      bv[g] = (qi < n_quads && bq != nullptr) ? bq[qi] : Raw{};
+    for (int qi = threadIdx.x; qi < n_quads; qi += blockDim.x) {
+      s_w[qi] = wq[qi];
+      s_b[qi] = bq != nullptr ? bq[qi] : Raw{};
     }
   }
-  const PairState root = pair_tree(st, lane);
-  float2 mean = make_float2(__shfl_sync(0xFFFFFFFFu, root.mean.x, 0),
-                            __shfl_sync(0xFFFFFFFFu, root.mean.y, 0));
-  const float2 m2 = make_float2(__shfl_sync(0xFFFFFFFFu, root.m2.x, 0),
-                                __shfl_sync(0xFFFFFFFFu, root.m2.y, 0));
-  const float width = static_cast<float>(a.width);
-  const float2 rstd = make_float2(rsqrtf(__fadd_rn(__fdiv_rn(m2.x, width), a.eps)),
-                                  rsqrtf(__fadd_rn(__fdiv_rn(m2.y, width), a.eps)));
-  // the second pass reads the rounded residual back (residual_out, or x
-  // itself for a plain LayerNorm) unless the rows are held in registers
-  const Raw* src[2] = {has_update ? static_cast<const Raw*>(rq[0]) : xq[0],
-                       has_update ? static_cast<const Raw*>(rq[1]) : xq[1]};
-  // rows that are not held: each step's groups (and weight / bias groups)
-  // are re-read, the next step's while this one is normalised
-  Raw sv[kHold ? 1 : 2][2][4], wsv[kHold ? 1 : 2][4], bsv[kHold ? 1 : 2][4];
-  auto reload_step = [&](int k, int buf) {
-    if constexpr (!kHold) {
+  if constexpr (kPersist) __syncthreads();
+  const auto coef = [&](int k) {
+    return SiteCoef{s_coef[0][k][lane], s_coef[kPersist ? 1 : 0][k][lane],
+                    s_coef[kPersist ? 2 : 0][k][lane]};
+  };
+
+  for (; pair < pairs; pair += stride) {
+    load_step(pair, 0, 0);
+    const bool two = 2 * pair + 1 < a.rows;
+    const int64_t rows[2] = {row_of(pair, 0), row_of(pair, 1)};
+    bool zero_res[2], zero_norm[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const bool valid = a.mask == nullptr || a.mask[rows[i]] != 0;
+      zero_res[i] = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_RESIDUAL);
+      zero_norm[i] = !valid && (a.flags & B200TK_RLN_ZERO_INVALID_NORMALIZED);
+    }
+    const Raw* xq[2];
+    Raw* rq[2];
+    Raw* nq[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      xq[i] = reinterpret_cast<const Raw*>(static_cast<const T*>(a.x) + rows[i] * a.width);
+      rq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.residual_out) + rows[i] * a.width);
+      nq[i] = reinterpret_cast<Raw*>(static_cast<T*>(a.normalized_out) + rows[i] * a.width);
+    }
+
+    Raw held[kHold ? QPV * 4 : 1][2];  // the rounded residual groups of both rows, packed
+    PairMoments st[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) st[w] = PairMoments{splat(0.f), splat(0.f)};
+#pragma unroll
+    for (int k = 0; k < QPV; ++k) {
+      const int buf = k & 1;
+      if (k + 1 < QPV) load_step(pair, k + 1, buf ^ 1);
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         const int qi = lane + 32 * w + kAtenThreads * k;
-        const bool in = qi < n_quads;
-        sv[buf][0][w] = (in && !zero_res[0]) ? src[0][qi] : Raw{};
-        sv[buf][1][w] = (in && !zero_res[1]) ? src[1][qi] : Raw{};
-        if constexpr (!kPrefetch) {
-          wsv[buf][w] = in ? wq[qi] : Raw{};
-          bsv[buf][w] = (in && bq != nullptr) ? bq[qi] : Raw{};
+        if (qi >= n_quads) continue;
+        float r[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          Raw packed;  // the rounded residual (or x itself), packed
+          if (has_update) {
+            packed = zero_res[i] ? Raw{} : Q::add_round(xv[buf][i][w], uv[buf][i][w]);
+            if (i == 0 || two) rq[i][qi] = packed;
+          } else {
+            packed = zero_res[i] ? Raw{} : xv[buf][i][w];
+          }
+          Q::unpack(packed, r[i]);
+          if constexpr (kHold) held[k * 4 + w][i] = packed;
+        }
+        // fold: the count before element e of group k is 4k + e, so
+        // 1 / (4k + e + 1) folds to a correctly rounded constant
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 v = make_float2(r[0][e], r[1][e]);
+          const float2 delta = sub_x2(v, st[w].mean);
+          st[w].mean = fma_x2(delta, splat(1.f / static_cast<float>(4 * k + e + 1)), st[w].mean);
+          st[w].m2 = fma_x2(delta, sub_x2(v, st[w].mean), st[w].m2);
         }
       }
     }
-  };
-  reload_step(0, 0);
+    PairMoments root;
+    if constexpr (kPersist) {
+      root = pair_tree_c(st, lane, coef);
+    } else {
+      PairState leaf[4];
 #pragma unroll
-  for (int k = 0; k < QPV; ++k) {
-    const int buf = kHold ? 0 : (k & 1);
-    if (k + 1 < QPV) reload_step(k + 1, buf ^ 1);
+      for (int w = 0; w < 4; ++w) leaf[w] = PairState{st[w].mean, st[w].m2, leaf_count(w)};
+      const PairState r = pair_tree(leaf, lane);
+      root = PairMoments{r.mean, r.m2};
+    }
+    const float2 mean = make_float2(__shfl_sync(0xFFFFFFFFu, root.mean.x, 0),
+                                    __shfl_sync(0xFFFFFFFFu, root.mean.y, 0));
+    const float2 m2 = make_float2(__shfl_sync(0xFFFFFFFFu, root.m2.x, 0),
+                                  __shfl_sync(0xFFFFFFFFu, root.m2.y, 0));
+    const float2 rstd = make_float2(rsqrtf(__fadd_rn(__fdiv_rn(m2.x, width), a.eps)),
+                                    rsqrtf(__fadd_rn(__fdiv_rn(m2.y, width), a.eps)));
+    // the second pass reads the rounded residual back (residual_out, or x
+    // itself for a plain LayerNorm) unless the rows are held in registers
+    const Raw* src[2] = {has_update ? static_cast<const Raw*>(rq[0]) : xq[0],
+                         has_update ? static_cast<const Raw*>(rq[1]) : xq[1]};
+    // rows that are not held: each step's groups (and weight / bias groups)
+    // are re-read, the next step's while this one is normalised
+    Raw sv[kHold ? 1 : 2][2][4], wsv[kHold ? 1 : 2][4], bsv[kHold ? 1 : 2][4];
+    auto reload_step = [&](int k, int buf) {
+      if constexpr (!kHold) {
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const int qi = lane + 32 * w + kAtenThreads * k;
-      if (qi >= n_quads) continue;
-      float2 r[4];
-      float fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f};
-      {
-        float r0[4], r1[4];
-        if constexpr (kHold) {
-          Q::unpack(held[k * 4 + w][0], r0);
-          Q::unpack(held[k * 4 + w][1], r1);
-        } else {
-          Q::unpack(sv[buf][0][w], r0);
-          Q::unpack(sv[buf][1][w], r1);
+        for (int w = 0; w < 4; ++w) {
+          const int qi = lane + 32 * w + kAtenThreads * k;
+          const bool in = qi < n_quads;
+          sv[buf][0][w] = (in && !zero_res[0]) ? src[0][qi] : Raw{};
+          sv[buf][1][w] = (in && !zero_res[1]) ? src[1][qi] : Raw{};
+          if constexpr (!kPrefetch) {
+            wsv[buf][w] = in ? wq[qi] : Raw{};
+            bsv[buf][w] = (in && bq != nullptr) ? bq[qi] : Raw{};
+          }
         }
+      }
+    };
+    reload_step(0, 0);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) r[e] = make_float2(r0[e], r1[e]);
-      }
-      if constexpr (kPrefetch) {
-        Q::unpack(wv[k * 4 + w], fw);
-        if (bq != nullptr) Q::unpack(bv[k * 4 + w], fb);
-      } else {
-        Q::unpack(wsv[buf][w], fw);
-        if (bq != nullptr) Q::unpack(bsv[buf][w], fb);
-      }
-      float o[2][4];
+    for (int k = 0; k < QPV; ++k) {
+      const int buf = kHold ? 0 : (k & 1);
+      if (k + 1 < QPV) reload_step(k + 1, buf ^ 1);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        // n = w * (rstd * (r - mean)) + b, both rows per instruction
-        const float2 c = mul_x2(rstd, sub_x2(r[e], mean));
-        const float2 n = bq != nullptr ? fma_x2(splat(fw[e]), c, splat(fb[e]))
-                                       : mul_x2(splat(fw[e]), c);
-        o[0][e] = tf32 ? round_tf32(n.x) : n.x;
-        o[1][e] = tf32 ? round_tf32(n.y) : n.y;
+      for (int w = 0; w < 4; ++w) {
+        const int qi = lane + 32 * w + kAtenThreads * k;
+        if (qi >= n_quads) continue;
+        float2 r[4];
+        float fw[4], fb[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          float r0[4], r1[4];
+          if constexpr (kHold) {
+            Q::unpack(held[k * 4 + w][0], r0);
+            Q::unpack(held[k * 4 + w][1], r1);
+          } else {
+            Q::unpack(sv[buf][0][w], r0);
+            Q::unpack(sv[buf][1][w], r1);
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) r[e] = make_float2(r0[e], r1[e]);
+        }
+        if constexpr (kPrefetch) {
+          Q::unpack(s_w[qi], fw);
+          if (bq != nullptr) Q::unpack(s_b[qi], fb);
+        } else {
+          Q::unpack(wsv[buf][w], fw);
+          if (bq != nullptr) Q::unpack(bsv[buf][w], fb);
+        }
+        float o[2][4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // n = w * (rstd * (r - mean)) + b, both rows per instruction
+          const float2 c = mul_x2(rstd, sub_x2(r[e], mean));
+          const float2 n = bq != nullptr ? fma_x2(splat(fw[e]), c, splat(fb[e]))
+                                         : mul_x2(splat(fw[e]), c);
+          o[0][e] = tf32 ? round_tf32(n.x) : n.x;
+          o[1][e] = tf32 ? round_tf32(n.y) : n.y;
+        }
+        if (zero_norm[0]) o[0][0] = o[0][1] = o[0][2] = o[0][3] = 0.f;
+        if (zero_norm[1]) o[1][0] = o[1][1] = o[1][2] = o[1][3] = 0.f;
+        nq[0][qi] = Q::pack(o[0]);
+        if (two) nq[1][qi] = Q::pack(o[1]);
       }
-      if (zero_norm[0]) o[0][0] = o[0][1] = o[0][2] = o[0][3] = 0.f;
-      if (zero_norm[1]) o[1][0] = o[1][1] = o[1][2] = o[1][3] = 0.f;
-      nq[0][qi] = Q::pack(o[0]);
-      if (two) nq[1][qi] = Q::pack(o[1]);
     }
   }
+}
+
+int current_sm_count();
+
+// Resident CTAs per SM of one Welford instantiation (occupancy query, once).
+template <typename T, int QPV>
+int welford_ctas_per_sm() {
+  static std::atomic<int> cached{0};
+  int n = cached.load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rln_welford_kernel<T, QPV>,
+                                                      32 * kWelfordWarpsPerCta, 0) != cudaSuccess ||
+        n < 1) {
+      (void)cudaGetLastError();
+      n = 1;
+    }
+    cached.store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+template <typename T, int QPV>
+cudaError_t launch_welford_q(const RlnArgs& a, cudaStream_t stream) {
+  const int64_t pairs = (a.rows + 1) / 2;
+  int64_t grid = (pairs + kWelfordWarpsPerCta - 1) / kWelfordWarpsPerCta;
+  if (QPV <= 2) {  // the persistent form (kPersist)
+    const int64_t resident =
+        static_cast<int64_t>(current_sm_count()) * welford_ctas_per_sm<T, QPV>();
+    if (grid > resident) grid = resident;
+  }
+  if (grid > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
+  rln_welford_kernel<T, QPV><<<static_cast<unsigned>(grid), 32 * kWelfordWarpsPerCta, 0, stream>>>(a);
+  return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t launch_welford(const RlnArgs& a, cudaStream_t stream) {
   const int64_t quads = a.width / 4;
   const int qpv = static_cast<int>((quads + kAtenThreads - 1) / kAtenThreads);
-  constexpr int kRowsPerCta = 2 * kWelfordWarpsPerCta;
-  const int64_t grid = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
-  if (grid > 0x7FFFFFFF) return cudaErrorInvalidConfiguration;
-  const unsigned g = static_cast<unsigned>(grid);
-  constexpr int kBlock = 32 * kWelfordWarpsPerCta;
   switch (qpv) {
-    case 1: rln_welford_kernel<T, 1><<<g, kBlock, 0, stream>>>(a); break;
-    case 2: rln_welford_kernel<T, 2><<<g, kBlock, 0, stream>>>(a); break;
-    case 3: rln_welford_kernel<T, 3><<<g, kBlock, 0, stream>>>(a); break;
-    case 4: rln_welford_kernel<T, 4><<<g, kBlock, 0, stream>>>(a); break;
-    case 5: rln_welford_kernel<T, 5><<<g, kBlock, 0, stream>>>(a); break;
-    case 6: rln_welford_kernel<T, 6><<<g, kBlock, 0, stream>>>(a); break;
-    case 7: rln_welford_kernel<T, 7><<<g, kBlock, 0, stream>>>(a); break;
-    case 8: rln_welford_kernel<T, 8><<<g, kBlock, 0, stream>>>(a); break;
+    case 1: return launch_welford_q<T, 1>(a, stream);
+    case 2: return launch_welford_q<T, 2>(a, stream);
+    case 3: return launch_welford_q<T, 3>(a, stream);
+    case 4: return launch_welford_q<T, 4>(a, stream);
+    case 5: return launch_welford_q<T, 5>(a, stream);
+    case 6: return launch_welford_q<T, 6>(a, stream);
+    case 7: return launch_welford_q<T, 7>(a, stream);
+    case 8: return launch_welford_q<T, 8>(a, stream);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 template <typename T, int VPT, int TPR>
