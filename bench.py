@@ -74,9 +74,9 @@ NCU_TRAFFIC = {
     # bf16 attention, one-pass schedule, C3 at batch 1: 425.9 MB read +
     # 117.1 MB written
     ("attention", "C3"): (543.0e6, 1),
-    # bf16 attention, two-pass schedule, C5 at batch 64: 151.1 MB read +
-    # 27.7 MB written (part of the output still in L2 at kernel end)
-    ("attention", "C5"): (178.8e6, 64),
+    # bf16 attention, row-resident schedule, C5 at batch 64: 151.4 MB read +
+    # 28.7 MB written (part of the output still in L2 at kernel end)
+    ("attention", "C5"): (180.1e6, 64),
     # fused FFN projection, TF32, full C2: 113.0 MB read + 218.4 MB written
     ("ffn", "C2"): (331.4e6, 8),
     # fused FFN projection, bf16, C5 at batch 128: 105.6 MB read + 344.8 MB
@@ -947,6 +947,46 @@ def run_attention_only(args) -> int:
     return 0
 
 
+def run_rln_only(args) -> int:
+    """Kernel-only timing of the fused residual add + LayerNorm at the
+    configuration's shape (rows = batch x seq, width d_model), for profiling:
+    W warm-up launches, then K launches timed with CUDA events (L2 flushed
+    before each). Prints one JSON line; not the bench contract's line."""
+    from transformer_opt.kernels import fused_residual_layer_norm
+
+    name = args.config
+    b, s, d, h, f, layers, causal, dt = CONFIGS[name]
+    dtype = DTYPES[dt]
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device).manual_seed(0)
+    rows = b * s
+    x, u = (torch.randn(rows, d, device=device, generator=gen).to(dtype) for _ in range(2))
+    w = (1 + 0.1 * torch.randn(d, device=device, generator=gen)).to(dtype)
+    bias = (0.1 * torch.randn(d, device=device, generator=gen)).to(dtype)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            fused_residual_layer_norm(x, u, w, bias, 1e-5)
+        times = []
+        for _ in range(args.steps):
+            flush.zero_()
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record()
+            fused_residual_layer_norm(x, u, w, bias, 1e-5)
+            end.record()
+            end.synchronize()
+            times.append(start.elapsed_time(end))
+    ms = statistics.median(times)
+    nbytes = 4.0 * rows * d * x.element_size()
+    print(json.dumps({
+        "kernel": "residual_layer_norm", "config": describe(name), "rows": rows,
+        "width": d, "dtype": DTYPE_TAG[dt], "ms": ms, "gbs": nbytes / (ms / 1000.0) / 1e9,
+        "launches": args.warmup + args.steps,
+    }), flush=True)
+    return 0
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -968,6 +1008,8 @@ def main() -> int:
                         help="time only the fused FFN projection kernel (profiling)")
     parser.add_argument("--attention-only", action="store_true",
                         help="time only the fused attention kernel (profiling)")
+    parser.add_argument("--rln-only", action="store_true",
+                        help="time only the fused residual + LayerNorm kernel (profiling)")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         parser.error("--warmup must be >= 3")
@@ -981,6 +1023,8 @@ def main() -> int:
         return run_ffn_only(args)
     if args.attention_only:
         return run_attention_only(args)
+    if args.rln_only:
+        return run_rln_only(args)
     return run_b200_arm(args)
 
 
