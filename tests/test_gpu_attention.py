@@ -149,6 +149,52 @@ def test_padding_mask_only_changes_tiles_it_masks(dim, dtype, causal):
     assert_within_contract(out[1:2], ref)
 
 
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("dim,dtype,seq,schedule", [
+    (64, torch.float32, 700, "auto"), (128, torch.float32, 700, "auto"),
+    (64, torch.bfloat16, 700, "two_pass"), (128, torch.bfloat16, 700, "one_pass"),
+    (128, torch.float16, 700, "two_pass"), (64, torch.bfloat16, 500, "resident"),
+    (64, torch.float16, 500, "resident"),
+])
+def test_key_tiles_wholly_past_the_padding_are_never_read(dim, dtype, seq, schedule, causal):
+    # Right padding: key tiles that lie entirely past a row's last valid key
+    # hold only zero probabilities, and the kernel neither loads nor
+    # multiplies them. NaN in those tiles (positions from the 128-key
+    # boundary after the last valid key on; every tile width divides 128)
+    # therefore leaves the output bit-identical; the tile holding the boundary
+    # is still read, so it gets large finite values that the mask zeroes.
+    torch.manual_seed(59)
+    batch = 5
+    q = torch.randn(batch, seq, 2, dim, device="cuda", dtype=dtype)
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    lengths = [seq, 131, 1, 0, 257]
+    mask = torch.arange(seq, device="cuda")[None, :] < torch.tensor(lengths, device="cuda")[:, None]
+    base = attention_fwd_with(q, k, v, mask, causal, schedule)
+    for b, n in enumerate(lengths):
+        k[b, n:] = 1e4
+        v[b, n:] = -1e4
+        end = -(-max(n, 1) // 128) * 128
+        k[b, end:] = float("nan")
+        v[b, end:] = float("nan")
+    out = attention_fwd_with(q, k, v, mask, causal, schedule)
+    assert torch.equal(out, base)
+    assert torch.equal(out[3], torch.zeros_like(out[3]))  # no valid key: zeros
+    if schedule == "one_pass":
+        return  # its rounding meets the rule on long rows, not on these (see its own tests)
+    with torch.inference_mode():
+        ref = oracle.reference_attention(q[[0, 1, 2, 4]], k[[0, 1, 2, 4]].nan_to_num(),
+                                         v[[0, 1, 2, 4]].nan_to_num(), mask[[0, 1, 2, 4]], causal)
+    assert_within_contract(out[[0, 1, 2, 4]], ref)
+
+
+def attention_fwd_with(q, k, v, mask, causal, schedule):
+    out = torch.empty_like(q)
+    with torch.inference_mode():
+        _native.attention_fwd(q, k, v, mask, out, causal, q.shape[-1] ** -0.5, schedule)
+    torch.cuda.synchronize()
+    return out
+
+
 @pytest.mark.parametrize("scale", [0.3, -0.125])
 @pytest.mark.parametrize("dim,dtype", [(64, torch.float32), (128, torch.float32), (64, torch.bfloat16)])
 def test_custom_and_negative_scales(dim, dtype, scale):

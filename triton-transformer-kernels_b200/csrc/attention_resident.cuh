@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
+  __shared__ int s_kv_end[HAS_MASK ? kMaxMaskBatches : 1];
+  const bool kv_bounds = HAS_MASK && p.batch <= kMaxMaskBatches;
+  if (kv_bounds) mask_key_bounds(p, s_kv_end);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -168,7 +171,8 @@ __global__ void __launch_bounds__(RrLayout::kThreads, 1)
     w.b = bh / p.heads;
     w.h = bh - w.b * p.heads;
     w.q0 = qt * BM;
-    const int kv_end = CAUSAL ? min(p.seq, w.q0 + BM) : p.seq;
+    int kv_end = CAUSAL ? min(p.seq, w.q0 + BM) : p.seq;
+    if (HAS_MASK && kv_bounds) kv_end = max(1, min(kv_end, s_kv_end[w.b]));
     w.n_kv = (kv_end + BN - 1) / BN;
     return w;
   };

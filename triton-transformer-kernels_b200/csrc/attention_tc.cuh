@@ -75,6 +75,41 @@ struct __align__(64) AttnTcParams {
   unsigned int* status;
 };
 
+// Key-padding bound of every batch row of the mask: one past its last valid
+// key (0 for a row without valid keys), computed by the whole CTA at set-up
+// into shared memory (launches of at most kMaxMaskBatches rows; larger ones
+// keep every key tile). Key tiles from that bound on hold only padding keys,
+// whose probabilities are exactly zero, so no role loads or multiplies them;
+// an item keeps at least one key tile, so a row without valid keys still
+// takes the all-masked path and yields zeros.
+constexpr int kMaxMaskBatches = 1024;
+__device__ __forceinline__ void mask_key_bounds(const AttnTcParams& p, int* end) {
+  const int warps = static_cast<int>(blockDim.x >> 5);
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  for (int b = warp; b < p.batch; b += warps) {
+    const uint8_t* row = p.mask + static_cast<int64_t>(b) * p.mask_sb;
+    int last = -1;
+    int n0 = 0;
+    if (p.mask_ss == 1 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+      // 16 bytes per lane and load; the highest nonzero byte of a word is
+      // (31 - clz(word)) / 8 (little-endian)
+      const int nv = p.seq >> 4;
+      for (int i = lane; i < nv; i += 32) {
+        const uint4 v = reinterpret_cast<const uint4*>(row)[i];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (w[q] != 0u) last = max(last, 16 * i + 4 * q + (31 - __clz(w[q])) / 8);
+      }
+      n0 = nv << 4;
+    }
+    for (int n = n0 + lane; n < p.seq; n += 32)
+      if (row[static_cast<int64_t>(n) * p.mask_ss] != 0) last = max(last, n);
+    last = __reduce_max_sync(0xFFFFFFFFu, last);
+    if (lane == 0) end[b] = last + 1;
+  }
+}
+
 template <typename T>
 struct ElemTraits;
 template <>
@@ -359,6 +394,9 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads
     tmem_alloc(smem_u32(tmem_slot), L::kTAlloc);
     tmem_relinquish();
   }
+  __shared__ int s_kv_end[HAS_MASK ? kMaxMaskBatches : 1];
+  const bool kv_bounds = HAS_MASK && p.batch <= kMaxMaskBatches;
+  if (kv_bounds) mask_key_bounds(p, s_kv_end);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -428,7 +466,8 @@ __global__ void __launch_bounds__(TcLayout<T, D, BN, KST, VST, NQ, OP>::kThreads
     w.b = bh / p.heads;
     w.h = bh - w.b * p.heads;
     w.q0 = qt * NQ * BM;
-    const int kv_end = CAUSAL ? min(p.seq, w.q0 + NQ * BM) : p.seq;
+    int kv_end = CAUSAL ? min(p.seq, w.q0 + NQ * BM) : p.seq;
+    if (HAS_MASK && kv_bounds) kv_end = max(1, min(kv_end, s_kv_end[w.b]));
     w.n_kv = (kv_end + BN - 1) / BN;
     w.n_s = kTwoPass ? 2 * w.n_kv : w.n_kv;
     return w;
