@@ -76,7 +76,7 @@ struct RlnArgs {
   int dtype;
   float eps;
   uint32_t flags;
-  unsigned int* status;  // device status word (bounded waits of the staged path)
+  unsigned int* status;  // device status word (the LayerNorm kernels have no waits to bound)
 };
 cudaError_t launch_residual_layer_norm(const RlnArgs& args, cudaStream_t stream);
 
