@@ -187,6 +187,29 @@ def test_key_tiles_wholly_past_the_padding_are_never_read(dim, dtype, seq, sched
     assert_within_contract(out[[0, 1, 2, 4]], ref)
 
 
+@pytest.mark.parametrize("dtype,schedule", [(torch.bfloat16, "two_pass"), (torch.bfloat16, "resident"),
+                                            (torch.float32, "auto")])
+def test_masked_launch_beyond_the_per_batch_bound_table(dtype, schedule):
+    # More batch rows than the kernels keep per-batch key bounds for (1024):
+    # every key tile is computed, and the result is the same as on a batch
+    # the table covers.
+    torch.manual_seed(61)
+    batch, seq = 1100, 200
+    q = torch.randn(batch, seq, 1, 64, device="cuda", dtype=dtype)
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    lengths = torch.randint(0, seq + 1, (batch,), device="cuda")
+    mask = torch.arange(seq, device="cuda")[None, :] < lengths[:, None]
+    out = attention_fwd_with(q, k, v, mask, False, schedule)
+    rows = [0, 1, 517, 1023, 1024, 1099]
+    part = attention_fwd_with(q[rows].contiguous(), k[rows].contiguous(), v[rows].contiguous(),
+                              mask[rows].contiguous(), False, schedule)
+    assert torch.equal(out[rows], part)
+    valid = [r for r in rows if int(lengths[r]) > 0]
+    with torch.inference_mode():
+        ref = oracle.reference_attention(q[valid], k[valid], v[valid], mask[valid], False)
+    assert_within_contract(out[valid], ref)
+
+
 def attention_fwd_with(q, k, v, mask, causal, schedule):
     out = torch.empty_like(q)
     with torch.inference_mode():
