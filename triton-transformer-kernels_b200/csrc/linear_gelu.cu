@@ -159,24 +159,32 @@ __device__ __forceinline__ float gelu_erf(float v) {
 // Stegun 7.1.26, erfc(x) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-x^2),
 // t = 1 / (1 + p x), |error| <= 1.5e-7 -- far below the output's rounding
 // (bf16: 2^-9 relative, fp16: 2^-12), at about half the instructions of
-// erff. Reciprocal and exponential are the hardware approximations.
-__device__ __forceinline__ float gelu_poly(float v) {
-  const float x = fabsf(v) * 0.70710678118654752f;
-  float t;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, x, 1.0f)));
-  float y = fmaf(t, 1.061405429f, -1.453152027f);
-  y = fmaf(t, y, 1.421413741f);
-  y = fmaf(t, y, -0.284496736f);
-  y = fmaf(t, y, 0.254829592f);
-  y *= t;
-  const float q = y * ex2_approx(x * x * -1.4426950408889634f);  // erfc(|v| / sqrt(2))
-  return 0.5f * v * (v >= 0.f ? 2.0f - q : q);
-}
-
-template <typename T>
-__device__ __forceinline__ float gelu_out(float v) {
-  if constexpr (std::is_same_v<T, float>) return gelu_erf(v);
-  else return gelu_poly(v);
+// erff. Reciprocal and exponential are the hardware approximations. Two
+// values at a time: the polynomial and the products run as paired fp32
+// operations (each half rounded as the scalar operation), the reciprocal and
+// the exponential on the MUFU.
+__device__ __forceinline__ void gelu_poly2(float& v0, float& v1) {
+  const float2 x = __fmul2_rn(make_float2(fabsf(v0), fabsf(v1)),
+                              make_float2(0.70710678118654752f, 0.70710678118654752f));
+  const float2 d = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), x, make_float2(1.0f, 1.0f));
+  float t0, t1;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(d.y));
+  const float2 t = make_float2(t0, t1);
+  float2 y = __ffma2_rn(t, make_float2(1.061405429f, 1.061405429f),
+                        make_float2(-1.453152027f, -1.453152027f));
+  y = __ffma2_rn(t, y, make_float2(1.421413741f, 1.421413741f));
+  y = __ffma2_rn(t, y, make_float2(-0.284496736f, -0.284496736f));
+  y = __ffma2_rn(t, y, make_float2(0.254829592f, 0.254829592f));
+  y = __fmul2_rn(y, t);
+  const float2 xx = __fmul2_rn(__fmul2_rn(x, x),
+                               make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 q = __fmul2_rn(y, make_float2(ex2_approx(xx.x), ex2_approx(xx.y)));
+  const float2 hv = __fmul2_rn(make_float2(0.5f, 0.5f), make_float2(v0, v1));
+  const float2 r = __fmul2_rn(hv, make_float2(v0 >= 0.f ? 2.0f - q.x : q.x,
+                                              v1 >= 0.f ? 2.0f - q.y : q.y));
+  v0 = r.x;
+  v1 = r.y;
 }
 
 // Four bias values starting at b (16-byte aligned for fp32, 8 for 16-bit).
@@ -475,7 +483,17 @@ __device__ __forceinline__ void linear_tc_body(const LgParams& p) {
         }
         if constexpr (EPI == kEpiGelu) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_out<T>(round_to<T>(v[j]));
+          for (int j = 0; j < 32; j += 2) {
+            if constexpr (std::is_same_v<T, float>) {
+              v[j] = gelu_erf(v[j]);
+              v[j + 1] = gelu_erf(v[j + 1]);
+            } else {
+              float a = round_to<T>(v[j]), b = round_to<T>(v[j + 1]);
+              gelu_poly2(a, b);
+              v[j] = a;
+              v[j + 1] = b;
+            }
+          }
         } else {
           uint32_t res[32 * sizeof(T) / 4] = {};
           if (row_in) load_residual32<T>(res_row, col0 + c * 32, p.n_out, res);
